@@ -1,0 +1,559 @@
+// One sm_100a attention kernel for every read of the paged KV cache:
+//   * paged GQA decode      (reference src/paged_gqa.cu:16-74),
+//   * packed-cache decode   (reference src/packed_decode.cu:16-61),
+//   * ancestor-only tree verification (reference src/tree_attention.cu:14-71).
+//
+// Work unit (one CTA): one request, one KV head, up to 8*RT query rows that
+// share that KV head, and one contiguous range of the request's "virtual
+// pages" (the prefix pages of the page table, followed for tree verification by
+// ceil(nodes/16) pages of draft tokens). A query row is (node, q-head of the
+// GQA group); decode has one node.
+//
+// Data path per CTA (160 threads):
+//   warp 4      TMA producer: for each stage of 4 pages it issues 4-D tiled
+//               bulk-tensor loads (one 16-token x 64-dim box per K or V half
+//               page, 128-byte swizzle) straight from the page table into a
+//               3-stage shared-memory ring, completing on an mbarrier.
+//   warps 0..3  consumers, arranged as RT row tiles x (4/RT) page groups. Per
+//               16-token page: S^T = K Q^T with mma.sync m16n8k16 (FP16 in,
+//               FP32 accumulate; K fragments by ldmatrix from the swizzled
+//               tile, Q fragments resident in registers), masking, an FP32
+//               online softmax in the log2 domain, then O^T += V^T P^T with P
+//               split into FP16 hi + lo halves (two MMAs) so the probabilities
+//               keep ~22 bits, i.e. the PV product is FP32-accurate.
+// End of CTA: the page groups' (m, l, O) states are merged in shared memory;
+// the CTA result is then either normalised and stored, written as a split
+// partial to global scratch, or merged across the CTAs of a thread-block
+// cluster through distributed shared memory (no scratch, no second launch).
+//
+// Numerics follow the reference: FP32 accumulation, scale 1/sqrt(D) (or the
+// caller's), empty sequences produce zeros.
+#pragma once
+
+#include <cmath>
+
+#include "bc_device.cuh"
+
+namespace bc {
+
+constexpr int kPageSize = 16;
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kPagesPerStage = 4;
+constexpr int kStages = 3;
+
+enum SplitMode : int { kSplitNone = 0, kSplitCluster = 1, kSplitGlobal = 2 };
+
+struct AttnParams {
+  int batch, hq, hkv, group, nodes;  // nodes == 1 for decode
+  int max_pages, physical_pages;
+  int rows;        // query rows per (request, KV head) = nodes * group
+  int row_chunks;  // CTAs along the rows: ceil(rows / (8 * RT))
+  int splits;      // CTAs along the virtual page range (gridDim.z)
+  int split_mode;  // SplitMode
+  int emit_partial;  // cluster/none mode: store (m, l, acc) per row instead of output
+  int slot_major;    // K/V maps are (D, 16, Hkv, P) instead of (D, Hkv, 16, P)
+  const __half* q;
+  const int* pages;
+  const int* lengths;
+  const int* parent;
+  void* out;
+  float* partial_a;
+  float* partial_ml;
+  float scale_log2;  // softmax scale * log2(e)
+  unsigned* err;
+};
+
+template <int D>
+struct AttnGeom {
+  static constexpr int kPageBytes = kPageSize * D * 2;  // K or V of one head, one page
+  static constexpr int kStageBytes = kPagesPerStage * 2 * kPageBytes;
+  static constexpr int kPipeBytes = kStages * kStageBytes;
+  static constexpr int kOStride = D + 4;  // padded FP32 row of the merge buffers
+  static constexpr int kMergeBytes =
+      (kConsumerWarps * 8 * kOStride + kConsumerWarps * 8 * 2 + 32 * kOStride + 32 * 2) * 4;
+  static_assert(kMergeBytes <= kPipeBytes, "merge buffers must fit in the pipeline ring");
+  static constexpr int kBarrierOffset = kPipeBytes;
+  static constexpr int kAncOffset = kPipeBytes + 2 * kStages * 8 + 16;
+  static size_t smem_bytes(bool tree, int nodes) {
+    return 1024 + size_t(kAncOffset) + (tree ? size_t(nodes) * 36 : 0);
+  }
+};
+
+__device__ __forceinline__ float shfl_xor_max(float x, int m) {
+  return fmaxf(x, __shfl_xor_sync(0xffffffffu, x, m));
+}
+
+template <int D, int RT, bool TREE, bool OUT_HALF>
+__global__ void __launch_bounds__(kThreads, 2)
+    attn_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap kmap,
+                const __grid_constant__ CUtensorMap vmap,
+                const __grid_constant__ CUtensorMap dkmap,
+                const __grid_constant__ CUtensorMap dvmap) {
+  using G = AttnGeom<D>;
+  constexpr int PG = kConsumerWarps / RT;  // page groups
+  constexpr int ROWS = 8 * RT;             // query rows per CTA
+  constexpr int NT = D / 16;               // QK k-steps == PV m-tiles
+  constexpr int KB = D / 64;               // 64-wide swizzled boxes per row
+  constexpr int PAGE = G::kPageBytes;
+  constexpr int STAGE = G::kStageBytes;
+  constexpr int OS = G::kOStride;
+  constexpr float kNegInf = -INFINITY;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kBarrierOffset);
+  uint64_t* empty = full + kStages;
+  uint32_t* anc = reinterpret_cast<uint32_t*>(smem + G::kAncOffset);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---- work unit
+  const int item = blockIdx.x;
+  const int rc = item % p.row_chunks;
+  const int bk = item / p.row_chunks;
+  const int b = bk % p.batch;
+  const int kvh = bk / p.batch;
+  const int split = blockIdx.z;
+
+  int len = p.lengths[b];
+  const int cap = p.max_pages * kPageSize;
+  if (len < 0 || len > cap) {
+    if (threadIdx.x == 0) atomicOr(p.err, kErrLength);
+    len = len < 0 ? 0 : cap;
+  }
+  const int npref = (len + kPageSize - 1) / kPageSize;
+  const int ndraft = TREE ? (p.nodes + kPageSize - 1) / kPageSize : 0;
+  const int nv = npref + ndraft;
+  const int per = (nv + p.splits - 1) / p.splits;
+  const int vbeg = min(nv, split * per);
+  const int vend = min(nv, vbeg + per);
+  const int nstages = (vend - vbeg + kPagesPerStage - 1) / kPagesPerStage;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  if constexpr (TREE) {
+    // Ancestor-or-self bit sets, one 256-bit row per node, walked over a
+    // shared-memory copy of this request's parent row. A walk longer than
+    // `nodes` steps (a cycle) or an index outside [0, nodes) stops the walk
+    // and flags the error.
+    int* par = reinterpret_cast<int*>(anc + p.nodes * 8);
+    for (int n = threadIdx.x; n < p.nodes; n += blockDim.x)
+      par[n] = __ldg(p.parent + size_t(b) * p.nodes + n);
+    __syncthreads();
+    for (int n = threadIdx.x; n < p.nodes; n += blockDim.x) {
+      uint32_t* row = anc + n * 8;  // written by this thread only
+#pragma unroll
+      for (int k = 0; k < 8; ++k) row[k] = 0u;
+      int cur = n, steps = 0;
+      while (cur >= 0) {
+        if (cur >= p.nodes || steps >= p.nodes) {
+          atomicOr(p.err, kErrParent);
+          break;
+        }
+        row[cur >> 5] |= 1u << (cur & 31);
+        cur = par[cur];
+        ++steps;
+      }
+    }
+  }
+  __syncthreads();
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    // The whole warp walks the stages; lane 0 issues the copies. Page ids are
+    // read 32 at a time with one coalesced load per lane, one group ahead, so
+    // the page-table latency never sits between two stages.
+    if (nstages > 0) {
+      if (lane == 0) {
+        prefetch_tmap(&kmap);
+        prefetch_tmap(&vmap);
+      }
+      const size_t prow = size_t(b) * p.max_pages;
+      auto load_id = [&](int v) -> int {
+        return (v < vend && v < npref) ? __ldg(p.pages + prow + v) : 0;
+      };
+      int cur_ids = load_id(vbeg + lane);
+      int next_ids = load_id(vbeg + 32 + lane);
+      int group = 0;
+      for (int i = 0; i < nstages; ++i) {
+        const int slot = i % kStages;
+        if (i >= kStages) {
+          const bool ok = mbar_wait(&empty[slot], ((i / kStages) - 1) & 1);
+          if (!__all_sync(0xffffffffu, ok)) {
+            if (lane == 0) atomicOr(p.err, kErrTimeout);
+            break;
+          }
+        }
+        const int v0 = vbeg + i * kPagesPerStage;
+        if (v0 - vbeg >= 32 * (group + 1)) {
+          ++group;
+          cur_ids = next_ids;
+          next_ids = load_id(vbeg + 32 * (group + 1) + lane);
+        }
+        const int np = min(kPagesPerStage, vend - v0);
+        const int off = v0 - vbeg - 32 * group;
+        int ids[kPagesPerStage];
+#pragma unroll
+        for (int j = 0; j < kPagesPerStage; ++j) ids[j] = __shfl_sync(0xffffffffu, cur_ids, off + j);
+        if (lane == 0) {
+          uint8_t* st = smem + slot * STAGE;
+          mbar_arrive_expect_tx(&full[slot], uint32_t(np * 2 * PAGE));
+#pragma unroll
+          for (int j = 0; j < kPagesPerStage; ++j) {
+            if (j >= np) break;
+            const int v = v0 + j;
+            uint8_t* dk = st + j * 2 * PAGE;
+            uint8_t* dv = dk + PAGE;
+            if (v < npref) {
+              const int phys = ids[j];
+              // Out-of-pool ids read as zeros (TMA out-of-bounds fill).
+              if (phys < 0 || phys >= p.physical_pages) atomicOr(p.err, kErrPageRange);
+              const int c1 = p.slot_major ? 0 : kvh, c2 = p.slot_major ? kvh : 0;
+#pragma unroll
+              for (int kb = 0; kb < KB; ++kb) {
+                tma_load_4d(dk + kb * 2048, &kmap, &full[slot], kb * 64, c1, c2, phys);
+                tma_load_4d(dv + kb * 2048, &vmap, &full[slot], kb * 64, c1, c2, phys);
+              }
+            } else if constexpr (TREE) {
+              const int n0 = (v - npref) * kPageSize;  // nodes >= `nodes` read as zeros
+#pragma unroll
+              for (int kb = 0; kb < KB; ++kb) {
+                tma_load_4d(dk + kb * 2048, &dkmap, &full[slot], kb * 64, kvh, n0, b);
+                tma_load_4d(dv + kb * 2048, &dvmap, &full[slot], kb * 64, kvh, n0, b);
+              }
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ consumers
+    const int rt = warp % RT;
+    const int pg = warp / RT;
+    const int g = lane >> 2;
+    const int tq = lane & 3;
+
+    // Q^T fragments (B operand): query row g of this warp's 8-row tile.
+    uint32_t qf[NT][2];
+    {
+      const int r = rc * ROWS + rt * 8 + g;
+      if (r < p.rows) {
+        const int node = r / p.group, hh = r % p.group;
+        const __half* qp =
+            p.q + ((size_t(b) * p.nodes + node) * p.hq + size_t(kvh) * p.group + hh) * D;
+#pragma unroll
+        for (int ks = 0; ks < NT; ++ks) {
+          qf[ks][0] = *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 2 * tq);
+          qf[ks][1] = *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 2 * tq + 8);
+        }
+      } else {
+#pragma unroll
+        for (int ks = 0; ks < NT; ++ks) qf[ks][0] = qf[ks][1] = 0u;
+      }
+    }
+    // This lane's two rows (columns of S^T): r0 and r0 + 1.
+    const int r0 = rc * ROWS + rt * 8 + 2 * tq;
+    const bool rv0 = r0 < p.rows, rv1 = r0 + 1 < p.rows;
+    const uint32_t* anc0 = nullptr;
+    const uint32_t* anc1 = nullptr;
+    if constexpr (TREE) {
+      anc0 = anc + (rv0 ? r0 / p.group : 0) * 8;
+      anc1 = anc + (rv1 ? (r0 + 1) / p.group : 0) * 8;
+    }
+
+    float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
+    float o[NT][4];
+#pragma unroll
+    for (int mt = 0; mt < NT; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+    // Lane-constant parts of the ldmatrix addresses (128-byte swizzle: the
+    // 16-byte chunk c of row t sits at chunk c ^ (t & 7)).
+    const int tk = (lane & 7) + ((lane >> 3) & 1) * 8;
+    const int ck = lane >> 4;
+    const int tv = (lane & 7) + (lane >> 4) * 8;
+    const int cv = (lane >> 3) & 1;
+
+    for (int i = 0; i < nstages; ++i) {
+      const int slot = i % kStages;
+      if (!mbar_wait(&full[slot], (i / kStages) & 1)) {
+        if (lane == 0) atomicOr(p.err, kErrTimeout);
+        break;
+      }
+      uint8_t* st = smem + slot * STAGE;
+#pragma unroll 1
+      for (int j = pg; j < kPagesPerStage; j += PG) {
+        const int v = vbeg + i * kPagesPerStage + j;
+        if (v >= vend) break;
+        const uint32_t kbase = smem_u32(st + j * 2 * PAGE);
+        const uint32_t vbase = kbase + PAGE;
+
+        // S^T[16 tokens x 8 rows] = K Q^T
+        float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < NT; ++ks) {
+          const int c = 2 * ks + ck;
+          uint32_t a[4];
+          ldsm_x4(kbase + (c >> 3) * 2048 + tk * 128 + (((c & 7) ^ (tk & 7)) << 4), a);
+          if (ks & 1)
+            mma_16816(s2, a, qf[ks][0], qf[ks][1]);
+          else
+            mma_16816(s, a, qf[ks][0], qf[ks][1]);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[c] += s2[c];
+
+        // Validity of (token g | g+8) x (row r0 | r0+1).
+        bool va, vb, vc, vd;
+        int vcount = kPageSize;
+        if (v < npref) {
+          vcount = min(kPageSize, len - v * kPageSize);
+          const bool t0 = g < vcount, t1 = g + 8 < vcount;
+          va = t0 && rv0;
+          vb = t0 && rv1;
+          vc = t1 && rv0;
+          vd = t1 && rv1;
+        } else {
+          const int n0 = (v - npref) * kPageSize + g;  // draft node of token g
+          const int bit = n0 & 31;
+          const uint32_t w0 = rv0 ? anc0[n0 >> 5] : 0u;
+          const uint32_t w1 = rv1 ? anc1[n0 >> 5] : 0u;
+          va = (w0 >> bit) & 1u;
+          vb = (w1 >> bit) & 1u;
+          vc = (w0 >> (bit + 8)) & 1u;
+          vd = (w1 >> (bit + 8)) & 1u;
+        }
+        const float x0 = va ? s[0] * p.scale_log2 : kNegInf;
+        const float x1 = vb ? s[1] * p.scale_log2 : kNegInf;
+        const float x2 = vc ? s[2] * p.scale_log2 : kNegInf;
+        const float x3 = vd ? s[3] * p.scale_log2 : kNegInf;
+
+        // Online softmax (log2 domain); l stays a per-lane partial sum.
+        float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+        mx0 = shfl_xor_max(mx0, 4);
+        mx1 = shfl_xor_max(mx1, 4);
+        mx0 = shfl_xor_max(mx0, 8);
+        mx1 = shfl_xor_max(mx1, 8);
+        mx0 = shfl_xor_max(mx0, 16);
+        mx1 = shfl_xor_max(mx1, 16);
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float base0 = mn0 == kNegInf ? 0.f : mn0;
+        const float base1 = mn1 == kNegInf ? 0.f : mn1;
+        const float al0 = fast_exp2(m0 - base0), al1 = fast_exp2(m1 - base1);
+        const float p0 = fast_exp2(x0 - base0), p1 = fast_exp2(x1 - base1);
+        const float p2 = fast_exp2(x2 - base0), p3 = fast_exp2(x3 - base1);
+        m0 = mn0;
+        m1 = mn1;
+        l0 = l0 * al0 + (p0 + p2);
+        l1 = l1 * al1 + (p1 + p3);
+#pragma unroll
+        for (int mt = 0; mt < NT; ++mt) {
+          o[mt][0] *= al0;
+          o[mt][1] *= al1;
+          o[mt][2] *= al0;
+          o[mt][3] *= al1;
+        }
+
+        // P^T fragments (B operand) as FP16 hi + lo, transposed in registers.
+        uint32_t h0, q0, h1, q1;
+        split_half2(p0, p1, h0, q0);  // tokens g     x rows (r0, r0+1)
+        split_half2(p2, p3, h1, q1);  // tokens g + 8 x rows (r0, r0+1)
+        const uint32_t bh0 = movmatrix_trans(h0), bh1 = movmatrix_trans(h1);
+        const uint32_t bl0 = movmatrix_trans(q0), bl1 = movmatrix_trans(q1);
+
+        // Slots past the sequence end may hold anything: zero their V.
+        const bool partial = vcount < kPageSize;
+        uint32_t vm_lo = 0xffffffffu, vm_hi = 0xffffffffu;
+        if (partial) {
+          vm_lo = (2 * tq < vcount ? 0x0000ffffu : 0u) | (2 * tq + 1 < vcount ? 0xffff0000u : 0u);
+          vm_hi = (2 * tq + 8 < vcount ? 0x0000ffffu : 0u) |
+                  (2 * tq + 9 < vcount ? 0xffff0000u : 0u);
+        }
+        // O^T[D x 8 rows] += V^T P^T
+#pragma unroll
+        for (int mt = 0; mt < NT; ++mt) {
+          const int c = 2 * mt + cv;
+          uint32_t a[4];
+          ldsm_x4_trans(vbase + (c >> 3) * 2048 + tv * 128 + (((c & 7) ^ (tv & 7)) << 4), a);
+          if (partial) {
+            a[0] &= vm_lo;
+            a[1] &= vm_lo;
+            a[2] &= vm_hi;
+            a[3] &= vm_hi;
+          }
+          mma_16816(o[mt], a, bh0, bh1);
+          mma_16816(o[mt], a, bl0, bl1);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+
+    // Full l per row: sum the per-lane partials over the 8 lanes of a column.
+#pragma unroll
+    for (int m = 4; m <= 16; m <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, m);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, m);
+    }
+
+    // Every consumer is done with the ring: reuse it for the merge buffers.
+    named_barrier_sync(1, kConsumerWarps * 32);
+    float* mo = reinterpret_cast<float*>(smem);     // [warp][8][OS]
+    float* mml = mo + kConsumerWarps * 8 * OS;       // [warp][8][2]
+    float* wo = mo + warp * 8 * OS;
+#pragma unroll
+    for (int mt = 0; mt < NT; ++mt) {
+      wo[(2 * tq) * OS + mt * 16 + g] = o[mt][0];
+      wo[(2 * tq + 1) * OS + mt * 16 + g] = o[mt][1];
+      wo[(2 * tq) * OS + mt * 16 + g + 8] = o[mt][2];
+      wo[(2 * tq + 1) * OS + mt * 16 + g + 8] = o[mt][3];
+    }
+    if (g == 0) {
+      mml[(warp * 8 + 2 * tq) * 2 + 0] = m0;
+      mml[(warp * 8 + 2 * tq) * 2 + 1] = l0;
+      mml[(warp * 8 + 2 * tq + 1) * 2 + 0] = m1;
+      mml[(warp * 8 + 2 * tq + 1) * 2 + 1] = l1;
+    }
+    named_barrier_sync(1, kConsumerWarps * 32);
+  }
+
+  // ---- merge the page groups of this CTA, then finish by split mode
+  float* mo = reinterpret_cast<float*>(smem);
+  float* mml = mo + kConsumerWarps * 8 * OS;
+  float* fo = mml + kConsumerWarps * 8 * 2;  // [ROWS][OS] CTA result
+  float* fml = fo + 32 * OS;                  // [ROWS][2]   (m log2, l)
+  const int tid = threadIdx.x;
+  const bool to_cluster = p.split_mode == kSplitCluster;
+  const float ln2 = 0.69314718055994531f;
+
+  auto out_index = [&](int r, int d) -> size_t {
+    const int node = r / p.group, hh = r % p.group;
+    return ((size_t(b) * p.nodes + node) * p.hq + size_t(kvh) * p.group + hh) * D + d;
+  };
+  auto store_out = [&](int r, int d, float value) {
+    const size_t idx = out_index(r, d);
+    if constexpr (OUT_HALF)
+      reinterpret_cast<__half*>(p.out)[idx] = __float2half_rn(value);
+    else
+      reinterpret_cast<float*>(p.out)[idx] = value;
+  };
+  // Writes one finished row state (natural-log m) as a partial, or the output.
+  auto finish = [&](int rl, int d, float m, float l, float acc) {
+    const int r = rc * ROWS + rl;
+    if (r >= p.rows) return;
+    if (p.split_mode == kSplitGlobal || p.emit_partial) {
+      const int hh = r % p.group;
+      const size_t slot_row =
+          (p.split_mode == kSplitGlobal ? (size_t(split) * p.batch + b) : size_t(b)) * p.hq +
+          size_t(kvh) * p.group + hh;
+      p.partial_a[slot_row * D + d] = acc;
+      if (d == 0) {
+        p.partial_ml[slot_row * 2 + 0] = m == kNegInf ? kNegInf : m * ln2;
+        p.partial_ml[slot_row * 2 + 1] = l;
+      }
+    } else {
+      store_out(r, d, l > 0.f ? acc / l : 0.f);
+    }
+  };
+
+  if (tid < kConsumerWarps * 32) {
+    for (int e = tid; e < ROWS * D; e += kConsumerWarps * 32) {
+      const int rl = e / D, d = e % D;
+      const int rtl = rl >> 3, rr = rl & 7;
+      float mmax = kNegInf;
+#pragma unroll
+      for (int q = 0; q < PG; ++q) mmax = fmaxf(mmax, mml[((rtl + RT * q) * 8 + rr) * 2]);
+      float acc = 0.f, lsum = 0.f;
+      if (mmax != kNegInf) {
+#pragma unroll
+        for (int q = 0; q < PG; ++q) {
+          const int w = rtl + RT * q;
+          const float wt = fast_exp2(mml[(w * 8 + rr) * 2] - mmax);
+          acc += wt * mo[(w * 8 + rr) * OS + d];
+          lsum += wt * mml[(w * 8 + rr) * 2 + 1];
+        }
+      }
+      if (to_cluster) {
+        fo[rl * OS + d] = acc;
+        if (d == 0) {
+          fml[rl * 2 + 0] = mmax;
+          fml[rl * 2 + 1] = lsum;
+        }
+      } else {
+        finish(rl, d, mmax, lsum, acc);
+      }
+    }
+  }
+
+  if (to_cluster) {
+    __syncwarp();
+    // All CTAs of the cluster (the splits of this work unit) hold their result
+    // in shared memory; each CTA merges a slice of the elements by reading
+    // every CTA's state through distributed shared memory.
+    cluster_sync_all();
+    const uint32_t rank = cluster_ctarank();
+    const int csize = p.splits;
+    const uint32_t fo_addr = smem_u32(fo), fml_addr = smem_u32(fml);
+    for (int e = int(rank) * kThreads + tid; e < ROWS * D; e += csize * kThreads) {
+      const int rl = e / D, d = e % D;
+      float mmax = kNegInf;
+      for (int c = 0; c < csize; ++c)
+        mmax = fmaxf(mmax, ld_cluster_f32(map_to_rank(fml_addr + rl * 8, c)));
+      float acc = 0.f, lsum = 0.f;
+      if (mmax != kNegInf) {
+        for (int c = 0; c < csize; ++c) {
+          const float mc = ld_cluster_f32(map_to_rank(fml_addr + rl * 8, c));
+          const float wt = fast_exp2(mc - mmax);
+          lsum += wt * ld_cluster_f32(map_to_rank(fml_addr + rl * 8 + 4, c));
+          acc += wt * ld_cluster_f32(map_to_rank(fo_addr + (rl * OS + d) * 4, c));
+        }
+      }
+      finish(rl, d, mmax, lsum, acc);
+    }
+    cluster_sync_all();  // keep this CTA's shared memory alive for its readers
+  }
+}
+
+// FP32 merge of global split partials (reference src/paged_gqa.cu:76-106):
+// one warp per row; partial m is in natural-log units.
+template <int D>
+__global__ void __launch_bounds__(128)
+    merge_kernel(int rows, int splits, const float* __restrict__ pml,
+                 const float* __restrict__ pa, float* __restrict__ out) {
+  constexpr int R = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float mmax = -INFINITY;
+  for (int s = 0; s < splits; ++s) mmax = fmaxf(mmax, pml[(size_t(s) * rows + row) * 2]);
+  float acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = 0.f;
+  float* o = out + size_t(row) * D;
+  if (mmax == -INFINITY) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) o[r * 32 + lane] = 0.f;
+    return;
+  }
+  float denom = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const size_t sr = size_t(s) * rows + row;
+    const float w = __expf(pml[sr * 2] - mmax);
+    denom += w * pml[sr * 2 + 1];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] += w * pa[sr * D + r * 32 + lane];
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) o[r * 32 + lane] = acc[r] / denom;
+}
+
+}  // namespace bc

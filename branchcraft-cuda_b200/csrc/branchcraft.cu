@@ -1,0 +1,529 @@
+// Host side of libbranchcraft.so: argument validation (the reference's rules,
+// src/paged_gqa.cu:122-132, src/tree_attention.cu:93-122,
+// src/packed_decode.cu:64-82), TMA tensor-map encoding, launch-shape choice and
+// the extern "C" entry points declared in include/branchcraft.h.
+//
+// The library is stateless with respect to its callers: it allocates nothing,
+// launches only on the stream it is given and keeps just per-device caches of
+// immutable facts (SM count, the error-word address, which kernels had their
+// shared-memory limit raised).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <mutex>
+
+#include "bc_attn.cuh"
+#include "bc_commit.cuh"
+#include "branchcraft.h"
+
+namespace bc {
+
+// Per-device error word (BC_ERR_* bits), set by kernels with atomicOr.
+__device__ unsigned g_error_word;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr float kLog2e = 1.4426950408889634f;
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  return dev;
+}
+
+unsigned* error_word(int dev) {
+  static std::atomic<unsigned*> cache[kMaxDevices];
+  static std::mutex mu;
+  unsigned* p = cache[dev].load(std::memory_order_acquire);
+  if (p) return p;
+  std::lock_guard<std::mutex> lock(mu);
+  p = cache[dev].load(std::memory_order_relaxed);
+  if (!p) {
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_error_word) != cudaSuccess)
+      return nullptr;
+    cache[dev].store(p, std::memory_order_release);
+  }
+  return p;
+}
+
+int sm_count(int dev) {
+  static std::atomic<int> cache[kMaxDevices];
+  int n = cache[dev].load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1)
+    n = 148;
+  cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+// ------------------------------------------------------------ tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+// FP16 4-D map with a 64-element inner box and 128-byte swizzle.
+bool encode_map(CUtensorMap* map, const void* base, const uint64_t dims[4],
+                const uint64_t strides_bytes[3], const uint32_t box[4]) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  if (reinterpret_cast<uintptr_t>(base) % 16) return false;
+  for (int i = 0; i < 3; ++i)
+    if (strides_bytes[i] % 16 || strides_bytes[i] >= (uint64_t(1) << 40)) return false;
+  cuuint64_t gdim[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t gstr[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  cuuint32_t bdim[4] = {box[0], box[1], box[2], box[3]};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), gdim, gstr, bdim,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// K or V of a paged cache viewed as 4-D (D, heads, 16 slots, pages) — or
+// (D, 16 slots, heads, pages) when the slot stride is the smaller one — with
+// strides given in elements.
+bool encode_cache_map(CUtensorMap* map, const void* base, int dim, int heads, int pages,
+                      long long head_stride, long long slot_stride, long long block_stride,
+                      bool* slot_major) {
+  *slot_major = slot_stride < head_stride;
+  const uint64_t dims[4] = {uint64_t(dim), uint64_t(*slot_major ? 16 : heads),
+                            uint64_t(*slot_major ? heads : 16), uint64_t(pages)};
+  const uint64_t st[3] = {uint64_t(*slot_major ? slot_stride : head_stride) * 2,
+                          uint64_t(*slot_major ? head_stride : slot_stride) * 2,
+                          uint64_t(block_stride) * 2};
+  const uint32_t box[4] = {64, uint32_t(*slot_major ? 16 : 1), uint32_t(*slot_major ? 1 : 16), 1};
+  return encode_map(map, base, dims, st, box);
+}
+
+// Draft K or V [batch, nodes, heads, D] as 4-D (D, heads, nodes, batch).
+bool encode_draft_map(CUtensorMap* map, const void* base, int dim, int heads, int nodes,
+                      int batch) {
+  const uint64_t dims[4] = {uint64_t(dim), uint64_t(heads), uint64_t(nodes), uint64_t(batch)};
+  const uint64_t st[3] = {uint64_t(dim) * 2, uint64_t(heads) * dim * 2,
+                          uint64_t(nodes) * heads * dim * 2};
+  const uint32_t box[4] = {64, 1, 16, 1};
+  return encode_map(map, base, dims, st, box);
+}
+
+// ---------------------------------------------------------------- launches
+template <int D, int RT, bool TREE, bool OUT_HALF>
+cudaError_t launch_attn_t(const AttnParams& p, const CUtensorMap* maps, int items, int cluster,
+                          cudaStream_t stream) {
+  auto kern = attn_kernel<D, RT, TREE, OUT_HALF>;
+  const size_t smem = AttnGeom<D>::smem_bytes(TREE, p.nodes);
+  static std::atomic<uint64_t> configured{0};
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  if (!(configured.load(std::memory_order_relaxed) & (uint64_t(1) << dev))) {
+    const size_t most = AttnGeom<D>::smem_bytes(TREE, BC_MAX_NODES);
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(most));
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(uint64_t(1) << dev);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(items), 1, unsigned(p.splits));
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (cluster > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = unsigned(cluster);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, p, maps[0], maps[1], maps[2], maps[3]);
+}
+
+template <int D, bool TREE, bool OUT_HALF>
+cudaError_t launch_attn_rt(int rt, const AttnParams& p, const CUtensorMap* maps, int items,
+                           int cluster, cudaStream_t stream) {
+  switch (rt) {
+    case 1: return launch_attn_t<D, 1, TREE, OUT_HALF>(p, maps, items, cluster, stream);
+    case 2: return launch_attn_t<D, 2, TREE, OUT_HALF>(p, maps, items, cluster, stream);
+    default: return launch_attn_t<D, 4, TREE, OUT_HALF>(p, maps, items, cluster, stream);
+  }
+}
+
+cudaError_t launch_attn(int dim, int rt, bool tree, bool out_half, const AttnParams& p,
+                        const CUtensorMap* maps, int items, int cluster, cudaStream_t stream) {
+  if (dim == 64) {
+    if (tree) return out_half ? launch_attn_rt<64, true, true>(rt, p, maps, items, cluster, stream)
+                              : launch_attn_rt<64, true, false>(rt, p, maps, items, cluster, stream);
+    return out_half ? launch_attn_rt<64, false, true>(rt, p, maps, items, cluster, stream)
+                    : launch_attn_rt<64, false, false>(rt, p, maps, items, cluster, stream);
+  }
+  if (tree) return out_half ? launch_attn_rt<128, true, true>(rt, p, maps, items, cluster, stream)
+                            : launch_attn_rt<128, true, false>(rt, p, maps, items, cluster, stream);
+  return out_half ? launch_attn_rt<128, false, true>(rt, p, maps, items, cluster, stream)
+                  : launch_attn_rt<128, false, false>(rt, p, maps, items, cluster, stream);
+}
+
+// Row tiling: RT 8-row tiles per CTA (1, 2 or 4) and the CTAs along the rows.
+void row_tiling(int rows, int* rt, int* row_chunks) {
+  *rt = rows <= 8 ? 1 : rows <= 16 ? 2 : 4;
+  *row_chunks = (rows + 8 * *rt - 1) / (8 * *rt);
+}
+
+// Cluster split for one launch: split only to fill the GPU (two CTAs per SM),
+// keep at least 8 pages per CTA, and never exceed 8 CTAs (the portable cluster
+// size). Splitting large ragged batches for balance loses: a cluster needs all
+// of its CTAs free at once inside one GPC, which leaves SMs idle.
+int auto_cluster(long long items, int max_virtual_pages, int sms) {
+  int c = 1;
+  while (c < 8 && items * c < 2LL * sms) c *= 2;
+  while (c > 1 && (max_virtual_pages + c - 1) / c < 8) c /= 2;
+  return c;
+}
+
+bool basic_shape_ok(const bc_shape* s) {
+  return s && s->batch >= 1 && s->query_heads >= 1 && s->kv_heads >= 1 &&
+         s->query_heads % s->kv_heads == 0 && (s->dim == 64 || s->dim == 128) &&
+         s->max_pages >= 1 && s->physical_pages >= 1;
+}
+
+AttnParams base_params(const bc_shape* s, int nodes, unsigned* err) {
+  AttnParams p = {};
+  p.batch = s->batch;
+  p.hq = s->query_heads;
+  p.hkv = s->kv_heads;
+  p.group = s->query_heads / s->kv_heads;
+  p.nodes = nodes;
+  p.max_pages = s->max_pages;
+  p.physical_pages = s->physical_pages;
+  p.rows = nodes * p.group;
+  p.err = err;
+  return p;
+}
+
+// Paged decode core shared by bc_decode / bc_paged_decode / partial variants.
+// mode: kSplitNone / kSplitCluster / kSplitGlobal; emit_partial stores one
+// (m, l, acc) partial per (request, q-head).
+cudaError_t paged_decode_core(const bc_shape* s, const void* q, const void* k, const void* v,
+                              const int* pages, const int* lengths, void* out, bool out_half,
+                              float scale, int splits, int mode, bool emit_partial,
+                              float* partial_a, float* partial_ml, bool slot_major_hint,
+                              const CUtensorMap* kv_maps, cudaStream_t stream) {
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  unsigned* err = error_word(dev);
+  if (!err) return cudaErrorInvalidDevice;
+  AttnParams p = base_params(s, 1, err);
+  int rt = 1;
+  row_tiling(p.rows, &rt, &p.row_chunks);
+  p.splits = splits;
+  p.split_mode = mode;
+  p.emit_partial = emit_partial ? 1 : 0;
+  p.slot_major = slot_major_hint ? 1 : 0;
+  p.q = static_cast<const __half*>(q);
+  p.pages = pages;
+  p.lengths = lengths;
+  p.parent = nullptr;
+  p.out = out;
+  p.partial_a = partial_a;
+  p.partial_ml = partial_ml;
+  p.scale_log2 = scale * kLog2e;
+  CUtensorMap maps[4];
+  if (kv_maps) {
+    maps[0] = kv_maps[0];
+    maps[1] = kv_maps[1];
+  } else {
+    bool sm = false;
+    const long long hs = s->dim, ss = (long long)s->kv_heads * s->dim, bs = 16 * ss;
+    if (!encode_cache_map(&maps[0], k, s->dim, s->kv_heads, s->physical_pages, hs, ss, bs, &sm) ||
+        !encode_cache_map(&maps[1], v, s->dim, s->kv_heads, s->physical_pages, hs, ss, bs, &sm))
+      return cudaErrorInvalidValue;
+    p.slot_major = sm ? 1 : 0;
+  }
+  maps[2] = maps[0];
+  maps[3] = maps[1];
+  const long long items = (long long)s->kv_heads * s->batch * p.row_chunks;
+  if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
+  const int cluster = mode == kSplitCluster ? splits : 1;
+  cudaError_t e = launch_attn(s->dim, rt, false, out_half, p, maps, int(items), cluster, stream);
+  if (e != cudaSuccess || mode != kSplitGlobal || emit_partial) return e;
+  const int rows = s->batch * s->query_heads;
+  if (s->dim == 64)
+    merge_kernel<64><<<(rows + 3) / 4, 128, 0, stream>>>(rows, splits, partial_ml, partial_a,
+                                                         static_cast<float*>(out));
+  else
+    merge_kernel<128><<<(rows + 3) / 4, 128, 0, stream>>>(rows, splits, partial_ml, partial_a,
+                                                          static_cast<float*>(out));
+  return cudaGetLastError();
+}
+
+int pick_mode(int splits) { return splits <= 1 ? kSplitNone : splits <= 8 ? kSplitCluster : kSplitGlobal; }
+
+cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix_k,
+                      const void* prefix_v, const int* pages, const int* lengths,
+                      const void* draft_k, const void* draft_v, const int* parent, void* out,
+                      bool out_half, int nodes, cudaStream_t stream) {
+  if (!basic_shape_ok(s) || nodes < 1 || nodes > BC_MAX_NODES || !prefix_k || !prefix_v ||
+      !pages || !lengths || !draft_q || !draft_k || !draft_v || !parent || !out)
+    return cudaErrorInvalidValue;
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  unsigned* err = error_word(dev);
+  if (!err) return cudaErrorInvalidDevice;
+  AttnParams p = base_params(s, nodes, err);
+  int rt = 1;
+  row_tiling(p.rows, &rt, &p.row_chunks);
+  const long long items = (long long)s->kv_heads * s->batch * p.row_chunks;
+  if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
+  const int vmax = s->max_pages + (nodes + 15) / 16;
+  p.splits = auto_cluster(items, vmax, sm_count(dev));
+  p.split_mode = p.splits > 1 ? kSplitCluster : kSplitNone;
+  p.q = static_cast<const __half*>(draft_q);
+  p.pages = pages;
+  p.lengths = lengths;
+  p.parent = parent;
+  p.out = out;
+  p.scale_log2 = kLog2e / std::sqrt(float(s->dim));
+  CUtensorMap maps[4];
+  bool sm = false;
+  const long long hs = s->dim, ss = (long long)s->kv_heads * s->dim, bs = 16 * ss;
+  if (!encode_cache_map(&maps[0], prefix_k, s->dim, s->kv_heads, s->physical_pages, hs, ss, bs,
+                        &sm) ||
+      !encode_cache_map(&maps[1], prefix_v, s->dim, s->kv_heads, s->physical_pages, hs, ss, bs,
+                        &sm) ||
+      !encode_draft_map(&maps[2], draft_k, s->dim, s->kv_heads, nodes, s->batch) ||
+      !encode_draft_map(&maps[3], draft_v, s->dim, s->kv_heads, nodes, s->batch))
+    return cudaErrorInvalidValue;
+  p.slot_major = sm ? 1 : 0;
+  return launch_attn(s->dim, rt, true, out_half, p, maps, int(items),
+                     p.split_mode == kSplitCluster ? p.splits : 1, stream);
+}
+
+}  // namespace
+}  // namespace bc
+
+using namespace bc;
+
+extern "C" {
+
+int bc_decode(const bc_shape* s, const void* q, const void* k, const void* v, const int* pages,
+              const int* lengths, float* output, float* partial_a, float* partial_ml, int splits,
+              void* stream) {
+  if (!basic_shape_ok(s) || splits < 1 || splits > BC_MAX_SPLITS || !q || !k || !v || !pages ||
+      !lengths || !output || (splits > 1 && (!partial_a || !partial_ml)))
+    return cudaErrorInvalidValue;
+  return paged_decode_core(s, q, k, v, pages, lengths, output, false,
+                           1.0f / std::sqrt(float(s->dim)), splits, pick_mode(splits), false,
+                           partial_a, partial_ml, false, nullptr,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int bc_auto_splits(const bc_shape* s, int max_length, int sm_count_arg) {
+  if (!s || max_length < 512) return 1;
+  const int groups = s->kv_heads > 0 ? s->kv_heads : 1;
+  const int g = s->kv_heads > 0 ? s->query_heads / s->kv_heads : 1;
+  int rt = 1, chunks = 1;
+  row_tiling(g < 1 ? 1 : g, &rt, &chunks);
+  const long long base = (long long)(s->batch > 0 ? s->batch : 1) * groups * chunks;
+  const long long wanted = (2LL * (sm_count_arg > 0 ? sm_count_arg : 148) + base - 1) / base;
+  int splits = 1;
+  while (splits < wanted && splits < BC_MAX_SPLITS) splits *= 2;
+  while (splits > 1 && max_length / splits < 256) splits /= 2;
+  return splits;
+}
+
+int bc_paged_decode(const bc_shape* s, const void* q, const void* k, const void* v,
+                    const int* pages, const int* lengths, float* output, int splits,
+                    void* stream) {
+  if (!basic_shape_ok(s) || splits > 8 || !q || !k || !v || !pages || !lengths || !output)
+    return cudaErrorInvalidValue;
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  if (splits <= 0) {
+    int rt = 1, chunks = 1;
+    row_tiling(s->query_heads / s->kv_heads, &rt, &chunks);
+    splits = auto_cluster((long long)s->batch * s->kv_heads * chunks, s->max_pages, sm_count(dev));
+  }
+  return paged_decode_core(s, q, k, v, pages, lengths, output, false,
+                           1.0f / std::sqrt(float(s->dim)), splits, pick_mode(splits), false,
+                           nullptr, nullptr, false, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int bc_paged_decode_partial(const bc_shape* s, const void* q, const void* k, const void* v,
+                            const int* pages, const int* lengths, float* partial_ml,
+                            float* partial_a, int splits, void* stream) {
+  if (!basic_shape_ok(s) || splits > 8 || !q || !k || !v || !pages || !lengths || !partial_ml ||
+      !partial_a)
+    return cudaErrorInvalidValue;
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  if (splits <= 0) {
+    int rt = 1, chunks = 1;
+    row_tiling(s->query_heads / s->kv_heads, &rt, &chunks);
+    splits = auto_cluster((long long)s->batch * s->kv_heads * chunks, s->max_pages, sm_count(dev));
+  }
+  return paged_decode_core(s, q, k, v, pages, lengths, nullptr, false,
+                           1.0f / std::sqrt(float(s->dim)), splits,
+                           splits > 1 ? kSplitCluster : kSplitNone, true, partial_a, partial_ml,
+                           false, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int bc_tree_verify(const bc_shape* s, const void* draft_q, const void* prefix_k,
+                   const void* prefix_v, const int* pages, const int* lengths,
+                   const void* draft_k, const void* draft_v, const int* parent, float* output,
+                   int nodes, void* stream) {
+  return tree_core(s, draft_q, prefix_k, prefix_v, pages, lengths, draft_k, draft_v, parent,
+                   output, false, nodes, static_cast<cudaStream_t>(stream));
+}
+
+int bc_tree_verify_f16(const bc_shape* s, const void* draft_q, const void* prefix_k,
+                       const void* prefix_v, const int* pages, const int* lengths,
+                       const void* draft_k, const void* draft_v, const int* parent,
+                       void* output_f16, int nodes, void* stream) {
+  return tree_core(s, draft_q, prefix_k, prefix_v, pages, lengths, draft_k, draft_v, parent,
+                   output_f16, true, nodes, static_cast<cudaStream_t>(stream));
+}
+
+int bc_packed_decode_kv(const bc_shape* s, const void* q, const void* packed_kv,
+                        const int* pages, const int* lengths, void* output,
+                        long long block_stride, long long head_stride, long long slot_stride,
+                        long long kv_offset, float scale, int splits, void* stream) {
+  if (!basic_shape_ok(s) || !q || !packed_kv || !pages || !lengths || !output ||
+      block_stride < 1 || head_stride < 1 || slot_stride < 1 || !(scale > 0.f) || splits > 8)
+    return cudaErrorInvalidValue;
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  CUtensorMap maps[2];
+  bool sm = false;
+  const __half* kbase = static_cast<const __half*>(packed_kv);
+  if (!encode_cache_map(&maps[0], kbase, s->dim, s->kv_heads, s->physical_pages, head_stride,
+                        slot_stride, block_stride, &sm) ||
+      !encode_cache_map(&maps[1], kbase + kv_offset, s->dim, s->kv_heads, s->physical_pages,
+                        head_stride, slot_stride, block_stride, &sm))
+    return cudaErrorInvalidValue;
+  if (splits <= 0) {
+    int rt = 1, chunks = 1;
+    row_tiling(s->query_heads / s->kv_heads, &rt, &chunks);
+    splits = auto_cluster((long long)s->batch * s->kv_heads * chunks, s->max_pages, sm_count(dev));
+  }
+  return paged_decode_core(s, q, nullptr, nullptr, pages, lengths, output, true, scale, splits,
+                           splits > 1 ? kSplitCluster : kSplitNone, false, nullptr, nullptr, sm,
+                           maps, static_cast<cudaStream_t>(stream));
+}
+
+int bc_packed_decode(const bc_shape* s, const void* q, const void* packed_kv, const int* pages,
+                     const int* lengths, void* output, long long block_stride,
+                     long long head_stride, long long slot_stride, float scale, void* stream) {
+  if (!s) return cudaErrorInvalidValue;
+  return bc_packed_decode_kv(s, q, packed_kv, pages, lengths, output, block_stride, head_stride,
+                             slot_stride, s->dim, scale, 0, stream);
+}
+
+int bc_commit_path(const bc_shape* s, const void* draft_k, const void* draft_v, void* cache_k,
+                   void* cache_v, const int* path_nodes, const int* dest_pages,
+                   const int* dest_slots, int request, int nodes, int accepted, void* stream) {
+  if (!s || !draft_k || !draft_v || !cache_k || !cache_v || !path_nodes || !dest_pages ||
+      !dest_slots || request < 0 || request >= s->batch || nodes < 1 || accepted < 1 ||
+      accepted > nodes || s->kv_heads < 1 || (s->dim != 64 && s->dim != 128))
+    return cudaErrorInvalidValue;
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  unsigned* err = error_word(dev);
+  if (!err) return cudaErrorInvalidDevice;
+  const int row = s->kv_heads * s->dim;
+  const bool vec = ((reinterpret_cast<uintptr_t>(draft_k) | reinterpret_cast<uintptr_t>(draft_v) |
+                     reinterpret_cast<uintptr_t>(cache_k) | reinterpret_cast<uintptr_t>(cache_v)) %
+                    16) == 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int physical = s->physical_pages > 0 ? s->physical_pages : 0x7fffffff;
+  if (vec)
+    commit_kernel<true><<<accepted, 256, 0, st>>>(
+        row, s->batch, nodes, physical, static_cast<const __half*>(draft_k),
+        static_cast<const __half*>(draft_v), static_cast<__half*>(cache_k),
+        static_cast<__half*>(cache_v), nullptr, path_nodes, dest_pages, dest_slots, request, err);
+  else
+    commit_kernel<false><<<accepted, 256, 0, st>>>(
+        row, s->batch, nodes, physical, static_cast<const __half*>(draft_k),
+        static_cast<const __half*>(draft_v), static_cast<__half*>(cache_k),
+        static_cast<__half*>(cache_v), nullptr, path_nodes, dest_pages, dest_slots, request, err);
+  return cudaGetLastError();
+}
+
+int bc_commit_batch(const bc_shape* s, int nodes, const void* draft_k, const void* draft_v,
+                    void* cache_k, void* cache_v, const int* clone_src, const int* clone_dst,
+                    int nclones, const int* entry_request, const int* entry_node,
+                    const int* entry_page, const int* entry_slot, int nentries, void* stream) {
+  if (!s || !draft_k || !draft_v || !cache_k || !cache_v || nodes < 1 || nclones < 0 ||
+      nentries < 0 || s->kv_heads < 1 || (s->dim != 64 && s->dim != 128) ||
+      s->physical_pages < 1 || s->batch < 1 || (nclones > 0 && (!clone_src || !clone_dst)) ||
+      (nentries > 0 && (!entry_request || !entry_node || !entry_page || !entry_slot)))
+    return cudaErrorInvalidValue;
+  const uintptr_t mis = (reinterpret_cast<uintptr_t>(draft_k) | reinterpret_cast<uintptr_t>(draft_v) |
+                         reinterpret_cast<uintptr_t>(cache_k) | reinterpret_cast<uintptr_t>(cache_v)) %
+                        16;
+  if (mis) return cudaErrorInvalidValue;
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  unsigned* err = error_word(dev);
+  if (!err) return cudaErrorInvalidDevice;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int row = s->kv_heads * s->dim;
+  if (nclones > 0) {
+    clone_kernel<<<dim3(4, unsigned(nclones), 2), 256, 0, st>>>(
+        16 * row, s->physical_pages, static_cast<__half*>(cache_k), static_cast<__half*>(cache_v),
+        clone_src, clone_dst, err);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  if (nentries > 0)
+    commit_kernel<true><<<nentries, 256, 0, st>>>(
+        row, s->batch, nodes, s->physical_pages, static_cast<const __half*>(draft_k),
+        static_cast<const __half*>(draft_v), static_cast<__half*>(cache_k),
+        static_cast<__half*>(cache_v), entry_request, entry_node, entry_page, entry_slot, 0, err);
+  return cudaGetLastError();
+}
+
+int bc_merge_partials(int splits, int rows, int dim, const float* partial_ml,
+                      const float* partial_a, float* out, void* stream) {
+  if (splits < 1 || rows < 1 || (dim != 64 && dim != 128) || !partial_ml || !partial_a || !out)
+    return cudaErrorInvalidValue;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dim == 64)
+    merge_kernel<64><<<(rows + 3) / 4, 128, 0, st>>>(rows, splits, partial_ml, partial_a, out);
+  else
+    merge_kernel<128><<<(rows + 3) / 4, 128, 0, st>>>(rows, splits, partial_ml, partial_a, out);
+  return cudaGetLastError();
+}
+
+unsigned bc_last_device_error(int reset) {
+  const int dev = current_device();
+  if (dev < 0) return 0xffffffffu;
+  if (cudaDeviceSynchronize() != cudaSuccess) return 0xffffffffu;
+  unsigned word = 0;
+  if (cudaMemcpyFromSymbol(&word, g_error_word, sizeof(word)) != cudaSuccess) return 0xffffffffu;
+  if (reset) {
+    const unsigned zero = 0;
+    if (cudaMemcpyToSymbol(g_error_word, &zero, sizeof(zero)) != cudaSuccess) return 0xffffffffu;
+  }
+  return word;
+}
+
+const char* bc_version(void) { return "branchcraft-b200 0.1.0 (sm_100a)"; }
+
+}  // extern "C"

@@ -1,0 +1,171 @@
+/* branchcraft (B200 / sm_100a) — C ABI of the attention-over-paged-KV hot path.
+ *
+ * Every entry point takes plain pointers and sizes, launches on the caller's
+ * stream (NULL = legacy default stream), allocates nothing and returns a
+ * cudaError_t value: 0 on success, cudaErrorInvalidValue (1) for rejected
+ * arguments, otherwise the launch status. Asynchronous device faults surface at
+ * the caller's next synchronisation, as with any CUDA launch.
+ *
+ * All tensor pointers are DEVICE pointers. FP16 data is IEEE binary16; pass it
+ * as `const void*`. Layouts (row-major, innermost last):
+ *   q        [batch, query_heads, dim]                 (decode)
+ *   draft_q  [batch, nodes, query_heads, dim]          (tree verify)
+ *   k, v     [physical_pages, 16, kv_heads, dim]       (paged cache)
+ *   pages    [batch, max_pages] int32, lengths [batch] int32
+ *   draft_k, draft_v [batch, nodes, kv_heads, dim], parent [batch, nodes]
+ *
+ * Malformed indices found on the device (page ids outside [0, physical_pages),
+ * lengths outside [0, max_pages*16], cyclic or out-of-range parent pointers,
+ * commit destinations out of range) never fault: the access is skipped (a
+ * page outside the pool reads as zeros) and a bit is set in a per-device error
+ * word that bc_last_device_error() returns.
+ */
+#ifndef BRANCHCRAFT_H_
+#define BRANCHCRAFT_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BC_PAGE_SIZE 16
+#define BC_MAX_SPLITS 64
+#define BC_MAX_NODES 256
+
+/* Mirrors branchcraft::Shape (reference include/branchcraft.hpp:11-18). */
+typedef struct bc_shape {
+  int batch;
+  int query_heads;
+  int kv_heads;
+  int dim; /* 64 or 128 */
+  int max_pages;
+  int physical_pages;
+} bc_shape;
+
+/* Device error bits returned by bc_last_device_error(). */
+#define BC_ERR_PAGE_RANGE 1u
+#define BC_ERR_LENGTH 2u
+#define BC_ERR_PARENT 4u
+#define BC_ERR_TIMEOUT 8u
+#define BC_ERR_COMMIT_INDEX 16u
+
+/* Paged GQA split-KV decode with FP32 output [batch, query_heads, dim]; empty
+ * sequences give zeros. Replaces branchcraft::decode (reference
+ * include/branchcraft.hpp:39-40, src/paged_gqa.cu:122-132).
+ * splits in [1, BC_MAX_SPLITS] (the reference caps at 16). For splits > 1 the
+ * caller provides scratch exactly as the reference documents
+ * (include/branchcraft.hpp:32-36): partial_a = splits*B*Hq*D floats,
+ * partial_ml = splits*B*Hq*2 floats; both NULL is rejected for splits > 1.
+ * Splits <= 8 are merged on chip between the CTAs of one thread-block cluster
+ * and leave the scratch untouched; larger counts go through the scratch and a
+ * second (merge) launch. */
+int bc_decode(const bc_shape* shape, const void* q, const void* k, const void* v,
+              const int* pages, const int* lengths, float* output, float* partial_a,
+              float* partial_ml, int splits, void* stream);
+
+/* Split-count heuristic for bc_decode. Replaces branchcraft::auto_splits
+ * (reference include/branchcraft.hpp:41, src/paged_gqa.cu:134-142), retuned for
+ * this kernel's CTA shape (one CTA per request and KV head) and splits <= 64. */
+int bc_auto_splits(const bc_shape* shape, int max_length, int sm_count);
+
+/* Paged decode with the split count chosen by the library (splits <= 0) or
+ * given (1..8), merged on chip: needs no scratch. Not in the reference; backs
+ * the added `paged_decode` torch schema. */
+int bc_paged_decode(const bc_shape* shape, const void* q, const void* k, const void* v,
+                    const int* pages, const int* lengths, float* output, int splits,
+                    void* stream);
+
+/* Ancestor-only tree verification: every (request, node, q-head) attends to the
+ * request's paged prefix and to its own root-to-node chain of draft tokens
+ * (never siblings), scale 1/sqrt(dim). FP32 output [batch, nodes, Hq, D].
+ * nodes in [1, BC_MAX_NODES]. Parent pointers: -1 (root) or a node index;
+ * chains longer than `nodes` (cycles) and indices >= nodes set BC_ERR_PARENT.
+ * Replaces branchcraft::tree_verify (reference include/branchcraft.hpp:43-56,
+ * src/tree_attention.cu:93-105). shape->physical_pages bounds the page ids. */
+int bc_tree_verify(const bc_shape* shape, const void* draft_q, const void* prefix_k,
+                   const void* prefix_v, const int* pages, const int* lengths,
+                   const void* draft_k, const void* draft_v, const int* parent,
+                   float* output, int nodes, void* stream);
+
+/* As bc_tree_verify with FP16 output [batch, nodes, Hq, D] (FP32 accumulation,
+ * one rounding at the end). Not in the reference. */
+int bc_tree_verify_f16(const bc_shape* shape, const void* draft_q, const void* prefix_k,
+                       const void* prefix_v, const int* pages, const int* lengths,
+                       const void* draft_k, const void* draft_v, const int* parent,
+                       void* output_f16, int nodes, void* stream);
+
+/* Copy accepted draft nodes into physical KV slots:
+ * cache_{k,v}[dest_pages[i], dest_slots[i], :, :] =
+ *     draft_{k,v}[request, path_nodes[i], :, :]   for i < accepted.
+ * path_nodes / dest_pages / dest_slots are device arrays of length `accepted`.
+ * The caller updates page tables afterwards. Replaces branchcraft::commit_path
+ * (reference include/branchcraft.hpp:58-65, src/tree_attention.cu:107-122);
+ * shape->kv_heads, dim, batch and physical_pages are used. */
+int bc_commit_path(const bc_shape* shape, const void* draft_k, const void* draft_v,
+                   void* cache_k, void* cache_v, const int* path_nodes,
+                   const int* dest_pages, const int* dest_slots, int request, int nodes,
+                   int accepted, void* stream);
+
+/* A whole batch of copy-on-write commits in one call: first every page clone
+ * cache[clone_dst[c]] = cache[clone_src[c]] (K and V, all 16 slots), then every
+ * entry cache[entry_page[e], entry_slot[e]] = draft[entry_request[e],
+ * entry_node[e]]. All index arrays are device arrays. Not in the reference; it
+ * is the device half of PagedTreeCache.commit
+ * (python/branchcraft_torch/transaction.py:114-150) for many requests. */
+int bc_commit_batch(const bc_shape* shape, int nodes, const void* draft_k,
+                    const void* draft_v, void* cache_k, void* cache_v, const int* clone_src,
+                    const int* clone_dst, int nclones, const int* entry_request,
+                    const int* entry_node, const int* entry_page, const int* entry_slot,
+                    int nentries, void* stream);
+
+/* Decode straight from a packed cache with logical shape [P, Hkv, 16, 2D]:
+ * K of (page, kv head, slot) starts at page*block_stride + head*head_stride +
+ * slot*slot_stride elements and V at D elements after it; caller-supplied
+ * softmax scale; FP16 output [B, Hq, D], FP32 accumulation. Replaces
+ * branchcraft::packed_decode (reference include/branchcraft.hpp:67-74,
+ * src/packed_decode.cu:64-82). Strides must be multiples of 8 elements and the
+ * cache 16-byte aligned (the TMA rule); other strides are rejected. */
+int bc_packed_decode(const bc_shape* shape, const void* q, const void* packed_kv,
+                     const int* pages, const int* lengths, void* output,
+                     long long block_stride, long long head_stride, long long slot_stride,
+                     float scale, void* stream);
+
+/* As bc_packed_decode with an explicit K->V element offset (vLLM's
+ * [num_blocks, 2, 16, Hkv, D] cache: block_stride = 2*16*Hkv*D,
+ * head_stride = D, slot_stride = Hkv*D, kv_offset = 16*Hkv*D) and a split
+ * count (<= 0: chosen by the library; 1..8: merged on chip). Not in the
+ * reference. */
+int bc_packed_decode_kv(const bc_shape* shape, const void* q, const void* packed_kv,
+                        const int* pages, const int* lengths, void* output,
+                        long long block_stride, long long head_stride,
+                        long long slot_stride, long long kv_offset, float scale, int splits,
+                        void* stream);
+
+/* FP32 merge of split partial states into out [rows, dim]:
+ * partial_ml[(s*rows + r)*2 + {0,1}] = (m, l), m the natural-log running max,
+ * partial_a[(s*rows + r)*dim + d] the unnormalised accumulator. Rows whose m
+ * are all -inf give zeros. The same math as the reference merge_kernel
+ * (src/paged_gqa.cu:76-106); used after an all-gather of per-GPU partials. */
+int bc_merge_partials(int splits, int rows, int dim, const float* partial_ml,
+                      const float* partial_a, float* out, void* stream);
+
+/* As bc_paged_decode but always writing this call's un-merged state as one
+ * partial (m, l, acc) per (request, q-head) into partial_ml / partial_a
+ * (layout of bc_merge_partials with splits = 1, rows = B*Hq): the per-GPU half
+ * of a context split across GPUs. `splits` (<= 0 auto, 1..8) is the on-chip
+ * split inside this GPU. Not in the reference. */
+int bc_paged_decode_partial(const bc_shape* shape, const void* q, const void* k,
+                            const void* v, const int* pages, const int* lengths,
+                            float* partial_ml, float* partial_a, int splits, void* stream);
+
+/* Returns the current device's error word (BC_ERR_* bits; 0 = clean) after
+ * synchronising that device; reset != 0 clears it. */
+unsigned bc_last_device_error(int reset);
+
+/* Library version string. */
+const char* bc_version(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* BRANCHCRAFT_H_ */

@@ -1,0 +1,99 @@
+"""Tree verification through the C ABI: the reference's known answers
+(src/main.cu:252-262), random topological trees (BASELINE config 2 style) and
+the FP16-output variant."""
+import numpy as np
+import pytest
+import torch
+
+import bc_testutil as U
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def capi():
+    import bc_capi
+
+    return bc_capi
+
+
+def _run_tree(capi, shape, nodes, f, out_dtype=torch.float32):
+    s = capi.make_shape(*shape)
+    t = {n: U.to_dev(f[n]) for n in ("draft_q", "k", "v", "pages", "lengths", "draft_k",
+                                     "draft_v", "parent")}
+    out = torch.full(t["draft_q"].shape, float("nan"), device="cuda", dtype=out_dtype)
+    capi.tree_verify(s, t["draft_q"], t["k"], t["v"], t["pages"], t["lengths"], t["draft_k"],
+                     t["draft_v"], t["parent"], out, nodes)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+@pytest.mark.parametrize("case", range(len(U.TREE_CASES)))
+def test_reference_tree_cases(capi, case):
+    g = U.golden()
+    prefix, d, seed = U.TREE_CASES[case]
+    f = O.ref_tree_fixture(2, prefix, 7, d, seed)
+    assert U.digest(f["q"], f["k"], f["v"], f["pages"], f["lengths"], f["draft_q"],
+                    f["draft_k"], f["draft_v"], f["parent"]) == str(g[f"tree{case}_sha"])
+    got = _run_tree(capi, f["shape"].tuple(), 7, f)
+    err = U.max_abs(got, g[f"tree{case}_out"])
+    assert err <= 3e-4, f"max_abs_error={err}"
+    assert capi.last_device_error() == 0
+
+
+def _tree_fixture(rng, batch, prefix, nodes, hq=32, hkv=8, dim=128, parents="random",
+                  pool=None, shared=True):
+    f = U.paged_fixture(rng, batch, hq, hkv, dim, [prefix] * batch, pool_pages=pool,
+                        shared_prefix=shared)
+    f["draft_q"] = U.rand_half(rng, (batch, nodes, hq, dim))
+    f["draft_k"] = U.rand_half(rng, (batch, nodes, hkv, dim))
+    f["draft_v"] = U.rand_half(rng, (batch, nodes, hkv, dim))
+    f["parent"] = (U.random_tree_parents(rng, batch, nodes) if parents == "random"
+                   else U.binary_tree_parents(batch, nodes))
+    return f
+
+
+def _oracle_tree(f, nodes):
+    return O.tree(f["shape"], nodes, f["draft_q"], f["k"], f["v"], f["pages"], f["lengths"],
+                  f["draft_k"], f["draft_v"], f["parent"])
+
+
+@pytest.mark.parametrize("batch,prefix,nodes,hq,hkv,dim", [
+    (8, 2040, 7, 32, 8, 128),   # BASELINE config 2 shape
+    (3, 100, 1, 8, 2, 64),
+    (2, 0, 19, 8, 8, 64),       # no prefix; 19 nodes spans two draft pages
+    (2, 33, 63, 32, 8, 128),    # 63 nodes: 252 rows -> 8 row chunks
+    (1, 300, 256, 4, 2, 64),    # the node cap
+    (2, 47, 5, 40, 4, 128),     # GQA group 10 (> 8 rows per head)
+])
+def test_random_trees(capi, batch, prefix, nodes, hq, hkv, dim):
+    rng = np.random.default_rng(batch * 1000 + prefix + nodes)
+    f = _tree_fixture(rng, batch, prefix, nodes, hq, hkv, dim)
+    expected = _oracle_tree(f, nodes)
+    got = _run_tree(capi, f["shape"], nodes, f)
+    U.assert_close_baseline(got, expected)
+    assert U.max_abs(got, expected) < 2e-4
+
+
+def test_baseline_config1_fp16_output(capi):
+    """1 request, 2048-token prefix in a seeded permutation of a 256-page pool,
+    parents [-1,0,0,1,1,2,2], FP16 output checked at the BASELINE tolerance."""
+    rng = np.random.default_rng(2048)
+    f = _tree_fixture(rng, 1, 2048, 7, pool=256, parents="binary")
+    expected = _oracle_tree(f, 7)
+    got = _run_tree(capi, f["shape"], 7, f, out_dtype=torch.float16)
+    U.assert_close_baseline(got, expected)
+    got32 = _run_tree(capi, f["shape"], 7, f)
+    U.assert_close_baseline(got32, expected, atol=1e-4, rtol=1e-4)
+
+
+def test_non_topological_acyclic_parents(capi):
+    """The reference walks any acyclic parent chain; so does this kernel."""
+    rng = np.random.default_rng(77)
+    f = _tree_fixture(rng, 1, 20, 5, 8, 2, 64)
+    f["parent"] = np.array([[2, 2, -1, 0, 3]], np.int32)
+    expected = _oracle_tree(f, 5)
+    got = _run_tree(capi, f["shape"], 5, f)
+    assert U.max_abs(got, expected) < 2e-4
+    assert capi.last_device_error() == 0
