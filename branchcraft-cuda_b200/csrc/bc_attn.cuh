@@ -497,27 +497,52 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (to_cluster) {
     __syncwarp();
     // All CTAs of the cluster (the splits of this work unit) hold their result
-    // in shared memory; each CTA merges a slice of the elements by reading
-    // every CTA's state through distributed shared memory.
+    // in shared memory. Each thread of the cluster merges 4 consecutive
+    // elements of one row: it first issues every remote load it needs (m and
+    // l of each CTA, one float4 of accumulators per CTA) and only then
+    // combines, so the distributed-shared-memory latency is paid once.
     cluster_sync_all();
     const uint32_t rank = cluster_ctarank();
     const int csize = p.splits;
     const uint32_t fo_addr = smem_u32(fo), fml_addr = smem_u32(fml);
-    for (int e = int(rank) * kThreads + tid; e < ROWS * D; e += csize * kThreads) {
-      const int rl = e / D, d = e % D;
-      float mmax = kNegInf;
-      for (int c = 0; c < csize; ++c)
-        mmax = fmaxf(mmax, ld_cluster_f32(map_to_rank(fml_addr + rl * 8, c)));
-      float acc = 0.f, lsum = 0.f;
-      if (mmax != kNegInf) {
-        for (int c = 0; c < csize; ++c) {
-          const float mc = ld_cluster_f32(map_to_rank(fml_addr + rl * 8, c));
-          const float wt = fast_exp2(mc - mmax);
-          lsum += wt * ld_cluster_f32(map_to_rank(fml_addr + rl * 8 + 4, c));
-          acc += wt * ld_cluster_f32(map_to_rank(fo_addr + (rl * OS + d) * 4, c));
+    constexpr int kQuads = ROWS * D / 4;
+    for (int task = int(rank) * kThreads + tid; task < kQuads; task += csize * kThreads) {
+      const int rl = task / (D / 4), d4 = (task % (D / 4)) * 4;
+      if (rc * ROWS + rl >= p.rows) continue;
+      float mc[8], lc[8];
+      float4 oc[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        if (c < csize) {
+          const float2 ml = ld_cluster_f32x2(map_to_rank(fml_addr + rl * 8, c));
+          mc[c] = ml.x;
+          lc[c] = ml.y;
+          oc[c] = ld_cluster_f32x4(map_to_rank(fo_addr + (rl * OS + d4) * 4, c));
         }
       }
-      finish(rl, d, mmax, lsum, acc);
+      float mmax = kNegInf;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        if (c < csize) mmax = fmaxf(mmax, mc[c]);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float lsum = 0.f;
+      if (mmax != kNegInf) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          if (c < csize) {
+            const float wt = fast_exp2(mc[c] - mmax);
+            lsum += wt * lc[c];
+            acc.x += wt * oc[c].x;
+            acc.y += wt * oc[c].y;
+            acc.z += wt * oc[c].z;
+            acc.w += wt * oc[c].w;
+          }
+        }
+      }
+      finish(rl, d4 + 0, mmax, lsum, acc.x);
+      finish(rl, d4 + 1, mmax, lsum, acc.y);
+      finish(rl, d4 + 2, mmax, lsum, acc.z);
+      finish(rl, d4 + 3, mmax, lsum, acc.w);
     }
     cluster_sync_all();  // keep this CTA's shared memory alive for its readers
   }

@@ -10,6 +10,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdint>
@@ -17,6 +18,7 @@
 
 #include "bc_attn.cuh"
 #include "bc_commit.cuh"
+#include "bc_tree_mma.cuh"
 #include "branchcraft.h"
 
 namespace bc {
@@ -275,6 +277,90 @@ cudaError_t paged_decode_core(const bc_shape* s, const void* q, const void* k, c
 
 int pick_mode(int splits) { return splits <= 1 ? kSplitNone : splits <= 8 ? kSplitCluster : kSplitGlobal; }
 
+template <int D, bool PREC, bool OUT_HALF>
+cudaError_t configure_tree_kernel(int dev) {
+  static std::atomic<uint64_t> configured{0};
+  if (configured.load(std::memory_order_relaxed) & (uint64_t(1) << dev)) return cudaSuccess;
+  const size_t most = TreeGeom<D, PREC>::smem_bytes(BC_MAX_NODES);
+  cudaError_t e = cudaFuncSetAttribute(tree_mma_kernel<D, PREC, OUT_HALF>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(most));
+  if (e != cudaSuccess) return e;
+  configured.fetch_or(uint64_t(1) << dev);
+  return cudaSuccess;
+}
+
+// How many clusters of `c` CTAs of this kernel can be resident at once (one
+// CTA per SM at this shared-memory size); cached per device and size.
+template <int D, bool PREC, bool OUT_HALF>
+int tree_max_clusters(int dev, int c) {
+  static std::atomic<int> cache[kMaxDevices][4];
+  const int slot = c == 1 ? 0 : c == 2 ? 1 : c == 4 ? 2 : 3;
+  int n = cache[dev][slot].load(std::memory_order_relaxed);
+  if (n > 0) return n;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, unsigned(c));
+  cfg.blockDim = dim3(kTreeThreads, 1, 1);
+  cfg.dynamicSmemBytes = TreeGeom<D, PREC>::smem_bytes(BC_MAX_NODES);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = unsigned(c);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (configure_tree_kernel<D, PREC, OUT_HALF>(dev) != cudaSuccess ||
+      cudaOccupancyMaxActiveClusters(&n, tree_mma_kernel<D, PREC, OUT_HALF>, &cfg) !=
+          cudaSuccess ||
+      n < 1) {
+    cudaGetLastError();
+    n = sm_count(dev) / c;
+  }
+  cache[dev][slot].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+// Cluster split along the keys: fill the SMs, stay within one wave of
+// resident clusters, keep at least two key tiles per CTA.
+template <int D, bool PREC, bool OUT_HALF>
+int tree_splits(int dev, long long items, int tiles) {
+  const int sms = sm_count(dev);
+  int c = 1;
+  while (c < 8 && items * c < sms) c *= 2;
+  while (c > 1 && items > tree_max_clusters<D, PREC, OUT_HALF>(dev, c)) c /= 2;
+  while (c > 1 && (tiles + c - 1) / c < 2) c /= 2;
+  return c;
+}
+
+template <int D, bool PREC, bool OUT_HALF>
+cudaError_t launch_tree_t(TreeParams& p, const CUtensorMap* maps, int items, int tiles,
+                          size_t smem, cudaStream_t stream) {
+  auto kern = tree_mma_kernel<D, PREC, OUT_HALF>;
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  cudaError_t e = configure_tree_kernel<D, PREC, OUT_HALF>(dev);
+  if (e != cudaSuccess) return e;
+  p.splits = tree_splits<D, PREC, OUT_HALF>(dev, items, tiles);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(items), 1, unsigned(p.splits));
+  cfg.blockDim = dim3(kTreeThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (p.splits > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = unsigned(p.splits);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kern, p, maps[0], maps[1], maps[2], maps[3]);
+}
+
+// Tree verification on tcgen05. Requests are grouped R to a 128-row tile
+// (R = 128 / (nodes * group)); a group whose page tables match shares each
+// K/V tile of the prefix. FP32 output accumulates P as FP16 hi + lo (FP32-exact
+// products); FP16 output uses one FP16 P, matching its own rounding.
 cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix_k,
                       const void* prefix_v, const int* pages, const int* lengths,
                       const void* draft_k, const void* draft_v, const int* parent, void* out,
@@ -282,24 +368,39 @@ cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix
   if (!basic_shape_ok(s) || nodes < 1 || nodes > BC_MAX_NODES || !prefix_k || !prefix_v ||
       !pages || !lengths || !draft_q || !draft_k || !draft_v || !parent || !out)
     return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(draft_q) | reinterpret_cast<uintptr_t>(out)) % 16)
+    return cudaErrorInvalidValue;
   const int dev = current_device();
   if (dev < 0) return cudaErrorInvalidDevice;
   unsigned* err = error_word(dev);
   if (!err) return cudaErrorInvalidDevice;
-  AttnParams p = base_params(s, nodes, err);
-  int rt = 1;
-  row_tiling(p.rows, &rt, &p.row_chunks);
-  const long long items = (long long)s->kv_heads * s->batch * p.row_chunks;
+  TreeParams p = {};
+  p.batch = s->batch;
+  p.hq = s->query_heads;
+  p.hkv = s->kv_heads;
+  p.group = s->query_heads / s->kv_heads;
+  p.nodes = nodes;
+  p.max_pages = s->max_pages;
+  p.physical_pages = s->physical_pages;
+  p.rows_req = nodes * p.group;
+  int R = p.rows_req >= kTreeRows ? 1 : kTreeRows / p.rows_req;
+  R = std::min(R, std::min(s->batch, kTreeMaxReq));
+  p.req_per_block = R;
+  p.tiles_per_block = (R * p.rows_req + kTreeRows - 1) / kTreeRows;
+  p.blocks = (s->batch + R - 1) / R;
+  const long long items = (long long)s->kv_heads * p.blocks * p.tiles_per_block;
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
-  const int vmax = s->max_pages + (nodes + 15) / 16;
-  p.splits = auto_cluster(items, vmax, sm_count(dev));
-  p.split_mode = p.splits > 1 ? kSplitCluster : kSplitNone;
+  // Key tiles of one CTA before splitting: prefix tiles plus draft tiles.
+  const int npad = (nodes + 15) & ~15;
+  const int tiles = (s->max_pages * kPageSize + kTreeTile - 1) / kTreeTile +
+                    (R * npad + kTreeTile - 1) / kTreeTile;
   p.q = static_cast<const __half*>(draft_q);
   p.pages = pages;
   p.lengths = lengths;
   p.parent = parent;
   p.out = out;
   p.scale_log2 = kLog2e / std::sqrt(float(s->dim));
+  p.err = err;
   CUtensorMap maps[4];
   bool sm = false;
   const long long hs = s->dim, ss = (long long)s->kv_heads * s->dim, bs = 16 * ss;
@@ -310,9 +411,17 @@ cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix
       !encode_draft_map(&maps[2], draft_k, s->dim, s->kv_heads, nodes, s->batch) ||
       !encode_draft_map(&maps[3], draft_v, s->dim, s->kv_heads, nodes, s->batch))
     return cudaErrorInvalidValue;
-  p.slot_major = sm ? 1 : 0;
-  return launch_attn(s->dim, rt, true, out_half, p, maps, int(items),
-                     p.split_mode == kSplitCluster ? p.splits : 1, stream);
+  const int anc_rows = R * nodes;
+  if (s->dim == 64) {
+    const size_t smem = out_half ? TreeGeom<64, false>::smem_bytes(anc_rows)
+                                 : TreeGeom<64, true>::smem_bytes(anc_rows);
+    return out_half ? launch_tree_t<64, false, true>(p, maps, int(items), tiles, smem, stream)
+                    : launch_tree_t<64, true, false>(p, maps, int(items), tiles, smem, stream);
+  }
+  const size_t smem = out_half ? TreeGeom<128, false>::smem_bytes(anc_rows)
+                               : TreeGeom<128, true>::smem_bytes(anc_rows);
+  return out_half ? launch_tree_t<128, false, true>(p, maps, int(items), tiles, smem, stream)
+                  : launch_tree_t<128, true, false>(p, maps, int(items), tiles, smem, stream);
 }
 
 }  // namespace

@@ -97,3 +97,33 @@ def test_non_topological_acyclic_parents(capi):
     got = _run_tree(capi, f["shape"], 5, f)
     assert U.max_abs(got, expected) < 2e-4
     assert capi.last_device_error() == 0
+
+
+@pytest.mark.parametrize("nodes,hq,hkv", [(7, 32, 8), (3, 8, 8), (20, 16, 2)])
+def test_mixed_prefix_runs(capi, nodes, hq, hkv):
+    """Requests of one 128-row tile that share a prefix only in runs:
+    [A, A, B, C, C, C] (B shares A's pages but not its length; C is disjoint),
+    plus an empty prefix at the end."""
+    rng = np.random.default_rng(nodes * 31 + hq)
+    dim, pool = 64, 90
+    perm = rng.permutation(pool).astype(np.int32)
+    lens = np.array([300, 300, 290, 517, 517, 517, 0], np.int32)
+    batch = len(lens)
+    max_pages = 33
+    pages = np.full((batch, max_pages), -1, np.int32)
+    pages[0, :19] = perm[:19]
+    pages[1, :19] = perm[:19]
+    pages[2, :19] = perm[:19]
+    for b in (3, 4, 5):
+        pages[b, :33] = perm[19:52]
+    f = dict(shape=(batch, hq, hkv, dim, max_pages, pool), pages=pages, lengths=lens,
+             k=U.rand_half(rng, (pool, 16, hkv, dim)), v=U.rand_half(rng, (pool, 16, hkv, dim)),
+             draft_q=U.rand_half(rng, (batch, nodes, hq, dim)),
+             draft_k=U.rand_half(rng, (batch, nodes, hkv, dim)),
+             draft_v=U.rand_half(rng, (batch, nodes, hkv, dim)),
+             parent=U.random_tree_parents(rng, batch, nodes))
+    expected = _oracle_tree(f, nodes)
+    got = _run_tree(capi, f["shape"], nodes, f)
+    U.assert_close_baseline(got, expected)
+    assert U.max_abs(got, expected) < 2e-4
+    assert capi.last_device_error() == 0
