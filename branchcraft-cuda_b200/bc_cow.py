@@ -142,15 +142,23 @@ class PagePool:
 
     def plan_commit_batch(self, commits, nodes: int) -> CommitPlan:
         """commits: iterable of (request, path, draft_index) applied in order.
-        Validates like transaction.py:116-121."""
+        Validates like transaction.py:116-121. All or nothing: if any commit
+        of the batch fails (bad path, pool exhausted) the page state is left
+        exactly as it was and the error is raised."""
+        saved = (self.refcount.copy(), self.free.copy(),
+                 {r: p.copy() for r, p in self.pages.items()}, dict(self.lengths))
         plan = CommitPlan()
-        for request, path, draft_index in commits:
-            path = [int(n) for n in path]
-            if not path or len(path) > nodes:
-                raise ValueError("path is empty or longer than draft")
-            if any(n < 0 or n >= nodes for n in path):
-                raise ValueError("path node out of range")
-            self.plan_commit(request, len(path), plan, draft_index, path)
+        try:
+            for request, path, draft_index in commits:
+                path = [int(n) for n in path]
+                if not path or len(path) > nodes:
+                    raise ValueError("path is empty or longer than draft")
+                if any(n < 0 or n >= nodes for n in path):
+                    raise ValueError("path node out of range")
+                self.plan_commit(request, len(path), plan, draft_index, path)
+        except Exception:
+            self.refcount, self.free, self.pages, self.lengths = saved
+            raise
         return plan
 
     def page_table(self, requests, width: int | None = None, fill: int = -1):

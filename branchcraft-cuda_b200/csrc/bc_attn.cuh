@@ -1,13 +1,12 @@
-// One sm_100a attention kernel for every read of the paged KV cache:
+// The sm_100a decode kernel for every single-query read of the paged KV cache:
 //   * paged GQA decode      (reference src/paged_gqa.cu:16-74),
-//   * packed-cache decode   (reference src/packed_decode.cu:16-61),
-//   * ancestor-only tree verification (reference src/tree_attention.cu:14-71).
+//   * packed-cache decode   (reference src/packed_decode.cu:16-61).
+// (Tree verification, whose rows are dense enough for tcgen05, lives in
+// bc_tree_mma.cuh.)
 //
-// Work unit (one CTA): one request, one KV head, up to 8*RT query rows that
-// share that KV head, and one contiguous range of the request's "virtual
-// pages" (the prefix pages of the page table, followed for tree verification by
-// ceil(nodes/16) pages of draft tokens). A query row is (node, q-head of the
-// GQA group); decode has one node.
+// Work unit (one CTA): one request, one KV head, up to 8*RT query rows (the
+// q-heads of the GQA group that share that KV head) and one contiguous range of
+// the request's pages.
 //
 // Data path per CTA (160 threads):
 //   warp 4      TMA producer: for each stage of 4 pages it issues 4-D tiled
@@ -45,9 +44,9 @@ constexpr int kStages = 3;
 enum SplitMode : int { kSplitNone = 0, kSplitCluster = 1, kSplitGlobal = 2 };
 
 struct AttnParams {
-  int batch, hq, hkv, group, nodes;  // nodes == 1 for decode
+  int batch, hq, hkv, group;
   int max_pages, physical_pages;
-  int rows;        // query rows per (request, KV head) = nodes * group
+  int rows;        // query rows per (request, KV head) = group
   int row_chunks;  // CTAs along the rows: ceil(rows / (8 * RT))
   int splits;      // CTAs along the virtual page range (gridDim.z)
   int split_mode;  // SplitMode
@@ -56,7 +55,6 @@ struct AttnParams {
   const __half* q;
   const int* pages;
   const int* lengths;
-  const int* parent;
   void* out;
   float* partial_a;
   float* partial_ml;
@@ -74,22 +72,17 @@ struct AttnGeom {
       (kConsumerWarps * 8 * kOStride + kConsumerWarps * 8 * 2 + 32 * kOStride + 32 * 2) * 4;
   static_assert(kMergeBytes <= kPipeBytes, "merge buffers must fit in the pipeline ring");
   static constexpr int kBarrierOffset = kPipeBytes;
-  static constexpr int kAncOffset = kPipeBytes + 2 * kStages * 8 + 16;
-  static size_t smem_bytes(bool tree, int nodes) {
-    return 1024 + size_t(kAncOffset) + (tree ? size_t(nodes) * 36 : 0);
-  }
+  static constexpr size_t kSmemBytes = 1024 + size_t(kPipeBytes) + 2 * kStages * 8;
 };
 
 __device__ __forceinline__ float shfl_xor_max(float x, int m) {
   return fmaxf(x, __shfl_xor_sync(0xffffffffu, x, m));
 }
 
-template <int D, int RT, bool TREE, bool OUT_HALF>
+template <int D, int RT, bool OUT_HALF>
 __global__ void __launch_bounds__(kThreads, 2)
     attn_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ CUtensorMap kmap,
-                const __grid_constant__ CUtensorMap vmap,
-                const __grid_constant__ CUtensorMap dkmap,
-                const __grid_constant__ CUtensorMap dvmap) {
+                const __grid_constant__ CUtensorMap vmap) {
   using G = AttnGeom<D>;
   constexpr int PG = kConsumerWarps / RT;  // page groups
   constexpr int ROWS = 8 * RT;             // query rows per CTA
@@ -105,7 +98,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kBarrierOffset);
   uint64_t* empty = full + kStages;
-  uint32_t* anc = reinterpret_cast<uint32_t*>(smem + G::kAncOffset);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -125,8 +117,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     len = len < 0 ? 0 : cap;
   }
   const int npref = (len + kPageSize - 1) / kPageSize;
-  const int ndraft = TREE ? (p.nodes + kPageSize - 1) / kPageSize : 0;
-  const int nv = npref + ndraft;
+  const int nv = npref;
   const int per = (nv + p.splits - 1) / p.splits;
   const int vbeg = min(nv, split * per);
   const int vend = min(nv, vbeg + per);
@@ -139,31 +130,6 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&empty[s], kConsumerWarps);
     }
     fence_mbar_init();
-  }
-  if constexpr (TREE) {
-    // Ancestor-or-self bit sets, one 256-bit row per node, walked over a
-    // shared-memory copy of this request's parent row. A walk longer than
-    // `nodes` steps (a cycle) or an index outside [0, nodes) stops the walk
-    // and flags the error.
-    int* par = reinterpret_cast<int*>(anc + p.nodes * 8);
-    for (int n = threadIdx.x; n < p.nodes; n += blockDim.x)
-      par[n] = __ldg(p.parent + size_t(b) * p.nodes + n);
-    __syncthreads();
-    for (int n = threadIdx.x; n < p.nodes; n += blockDim.x) {
-      uint32_t* row = anc + n * 8;  // written by this thread only
-#pragma unroll
-      for (int k = 0; k < 8; ++k) row[k] = 0u;
-      int cur = n, steps = 0;
-      while (cur >= 0) {
-        if (cur >= p.nodes || steps >= p.nodes) {
-          atomicOr(p.err, kErrParent);
-          break;
-        }
-        row[cur >> 5] |= 1u << (cur & 31);
-        cur = par[cur];
-        ++steps;
-      }
-    }
   }
   __syncthreads();
 
@@ -223,13 +189,6 @@ __global__ void __launch_bounds__(kThreads, 2)
                 tma_load_4d(dk + kb * 2048, &kmap, &full[slot], kb * 64, c1, c2, phys);
                 tma_load_4d(dv + kb * 2048, &vmap, &full[slot], kb * 64, c1, c2, phys);
               }
-            } else if constexpr (TREE) {
-              const int n0 = (v - npref) * kPageSize;  // nodes >= `nodes` read as zeros
-#pragma unroll
-              for (int kb = 0; kb < KB; ++kb) {
-                tma_load_4d(dk + kb * 2048, &dkmap, &full[slot], kb * 64, kvh, n0, b);
-                tma_load_4d(dv + kb * 2048, &dvmap, &full[slot], kb * 64, kvh, n0, b);
-              }
             }
           }
         }
@@ -248,9 +207,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     {
       const int r = rc * ROWS + rt * 8 + g;
       if (r < p.rows) {
-        const int node = r / p.group, hh = r % p.group;
-        const __half* qp =
-            p.q + ((size_t(b) * p.nodes + node) * p.hq + size_t(kvh) * p.group + hh) * D;
+        const __half* qp = p.q + (size_t(b) * p.hq + size_t(kvh) * p.group + r) * D;
 #pragma unroll
         for (int ks = 0; ks < NT; ++ks) {
           qf[ks][0] = *reinterpret_cast<const uint32_t*>(qp + ks * 16 + 2 * tq);
@@ -264,12 +221,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     // This lane's two rows (columns of S^T): r0 and r0 + 1.
     const int r0 = rc * ROWS + rt * 8 + 2 * tq;
     const bool rv0 = r0 < p.rows, rv1 = r0 + 1 < p.rows;
-    const uint32_t* anc0 = nullptr;
-    const uint32_t* anc1 = nullptr;
-    if constexpr (TREE) {
-      anc0 = anc + (rv0 ? r0 / p.group : 0) * 8;
-      anc1 = anc + (rv1 ? (r0 + 1) / p.group : 0) * 8;
-    }
 
     float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
     float o[NT][4];
@@ -313,25 +264,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < 4; ++c) s[c] += s2[c];
 
         // Validity of (token g | g+8) x (row r0 | r0+1).
-        bool va, vb, vc, vd;
-        int vcount = kPageSize;
-        if (v < npref) {
-          vcount = min(kPageSize, len - v * kPageSize);
-          const bool t0 = g < vcount, t1 = g + 8 < vcount;
-          va = t0 && rv0;
-          vb = t0 && rv1;
-          vc = t1 && rv0;
-          vd = t1 && rv1;
-        } else {
-          const int n0 = (v - npref) * kPageSize + g;  // draft node of token g
-          const int bit = n0 & 31;
-          const uint32_t w0 = rv0 ? anc0[n0 >> 5] : 0u;
-          const uint32_t w1 = rv1 ? anc1[n0 >> 5] : 0u;
-          va = (w0 >> bit) & 1u;
-          vb = (w1 >> bit) & 1u;
-          vc = (w0 >> (bit + 8)) & 1u;
-          vd = (w1 >> (bit + 8)) & 1u;
-        }
+        const int vcount = min(kPageSize, len - v * kPageSize);
+        const bool t0 = g < vcount, t1 = g + 8 < vcount;
+        const bool va = t0 && rv0, vb = t0 && rv1, vc = t1 && rv0, vd = t1 && rv1;
         const float x0 = va ? s[0] * p.scale_log2 : kNegInf;
         const float x1 = vb ? s[1] * p.scale_log2 : kNegInf;
         const float x2 = vc ? s[2] * p.scale_log2 : kNegInf;
@@ -436,8 +371,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const float ln2 = 0.69314718055994531f;
 
   auto out_index = [&](int r, int d) -> size_t {
-    const int node = r / p.group, hh = r % p.group;
-    return ((size_t(b) * p.nodes + node) * p.hq + size_t(kvh) * p.group + hh) * D + d;
+    return (size_t(b) * p.hq + size_t(kvh) * p.group + r) * D + d;
   };
   auto store_out = [&](int r, int d, float value) {
     const size_t idx = out_index(r, d);
@@ -451,10 +385,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int r = rc * ROWS + rl;
     if (r >= p.rows) return;
     if (p.split_mode == kSplitGlobal || p.emit_partial) {
-      const int hh = r % p.group;
       const size_t slot_row =
           (p.split_mode == kSplitGlobal ? (size_t(split) * p.batch + b) : size_t(b)) * p.hq +
-          size_t(kvh) * p.group + hh;
+          size_t(kvh) * p.group + r;
       p.partial_a[slot_row * D + d] = acc;
       if (d == 0) {
         p.partial_ml[slot_row * 2 + 0] = m == kNegInf ? kNegInf : m * ln2;

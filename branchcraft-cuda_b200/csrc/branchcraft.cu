@@ -126,18 +126,17 @@ bool encode_draft_map(CUtensorMap* map, const void* base, int dim, int heads, in
 }
 
 // ---------------------------------------------------------------- launches
-template <int D, int RT, bool TREE, bool OUT_HALF>
+template <int D, int RT, bool OUT_HALF>
 cudaError_t launch_attn_t(const AttnParams& p, const CUtensorMap* maps, int items, int cluster,
                           cudaStream_t stream) {
-  auto kern = attn_kernel<D, RT, TREE, OUT_HALF>;
-  const size_t smem = AttnGeom<D>::smem_bytes(TREE, p.nodes);
+  auto kern = attn_kernel<D, RT, OUT_HALF>;
+  const size_t smem = AttnGeom<D>::kSmemBytes;
   static std::atomic<uint64_t> configured{0};
   const int dev = current_device();
   if (dev < 0) return cudaErrorInvalidDevice;
   if (!(configured.load(std::memory_order_relaxed) & (uint64_t(1) << dev))) {
-    const size_t most = AttnGeom<D>::smem_bytes(TREE, BC_MAX_NODES);
     cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(most));
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
     configured.fetch_or(uint64_t(1) << dev);
   }
@@ -155,31 +154,26 @@ cudaError_t launch_attn_t(const AttnParams& p, const CUtensorMap* maps, int item
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  return cudaLaunchKernelEx(&cfg, kern, p, maps[0], maps[1], maps[2], maps[3]);
+  return cudaLaunchKernelEx(&cfg, kern, p, maps[0], maps[1]);
 }
 
-template <int D, bool TREE, bool OUT_HALF>
+template <int D, bool OUT_HALF>
 cudaError_t launch_attn_rt(int rt, const AttnParams& p, const CUtensorMap* maps, int items,
                            int cluster, cudaStream_t stream) {
   switch (rt) {
-    case 1: return launch_attn_t<D, 1, TREE, OUT_HALF>(p, maps, items, cluster, stream);
-    case 2: return launch_attn_t<D, 2, TREE, OUT_HALF>(p, maps, items, cluster, stream);
-    default: return launch_attn_t<D, 4, TREE, OUT_HALF>(p, maps, items, cluster, stream);
+    case 1: return launch_attn_t<D, 1, OUT_HALF>(p, maps, items, cluster, stream);
+    case 2: return launch_attn_t<D, 2, OUT_HALF>(p, maps, items, cluster, stream);
+    default: return launch_attn_t<D, 4, OUT_HALF>(p, maps, items, cluster, stream);
   }
 }
 
-cudaError_t launch_attn(int dim, int rt, bool tree, bool out_half, const AttnParams& p,
+cudaError_t launch_attn(int dim, int rt, bool out_half, const AttnParams& p,
                         const CUtensorMap* maps, int items, int cluster, cudaStream_t stream) {
-  if (dim == 64) {
-    if (tree) return out_half ? launch_attn_rt<64, true, true>(rt, p, maps, items, cluster, stream)
-                              : launch_attn_rt<64, true, false>(rt, p, maps, items, cluster, stream);
-    return out_half ? launch_attn_rt<64, false, true>(rt, p, maps, items, cluster, stream)
-                    : launch_attn_rt<64, false, false>(rt, p, maps, items, cluster, stream);
-  }
-  if (tree) return out_half ? launch_attn_rt<128, true, true>(rt, p, maps, items, cluster, stream)
-                            : launch_attn_rt<128, true, false>(rt, p, maps, items, cluster, stream);
-  return out_half ? launch_attn_rt<128, false, true>(rt, p, maps, items, cluster, stream)
-                  : launch_attn_rt<128, false, false>(rt, p, maps, items, cluster, stream);
+  if (dim == 64)
+    return out_half ? launch_attn_rt<64, true>(rt, p, maps, items, cluster, stream)
+                    : launch_attn_rt<64, false>(rt, p, maps, items, cluster, stream);
+  return out_half ? launch_attn_rt<128, true>(rt, p, maps, items, cluster, stream)
+                  : launch_attn_rt<128, false>(rt, p, maps, items, cluster, stream);
 }
 
 // Row tiling: RT 8-row tiles per CTA (1, 2 or 4) and the CTAs along the rows.
@@ -205,16 +199,15 @@ bool basic_shape_ok(const bc_shape* s) {
          s->max_pages >= 1 && s->physical_pages >= 1;
 }
 
-AttnParams base_params(const bc_shape* s, int nodes, unsigned* err) {
+AttnParams base_params(const bc_shape* s, unsigned* err) {
   AttnParams p = {};
   p.batch = s->batch;
   p.hq = s->query_heads;
   p.hkv = s->kv_heads;
   p.group = s->query_heads / s->kv_heads;
-  p.nodes = nodes;
   p.max_pages = s->max_pages;
   p.physical_pages = s->physical_pages;
-  p.rows = nodes * p.group;
+  p.rows = p.group;
   p.err = err;
   return p;
 }
@@ -231,7 +224,7 @@ cudaError_t paged_decode_core(const bc_shape* s, const void* q, const void* k, c
   if (dev < 0) return cudaErrorInvalidDevice;
   unsigned* err = error_word(dev);
   if (!err) return cudaErrorInvalidDevice;
-  AttnParams p = base_params(s, 1, err);
+  AttnParams p = base_params(s, err);
   int rt = 1;
   row_tiling(p.rows, &rt, &p.row_chunks);
   p.splits = splits;
@@ -241,12 +234,11 @@ cudaError_t paged_decode_core(const bc_shape* s, const void* q, const void* k, c
   p.q = static_cast<const __half*>(q);
   p.pages = pages;
   p.lengths = lengths;
-  p.parent = nullptr;
   p.out = out;
   p.partial_a = partial_a;
   p.partial_ml = partial_ml;
   p.scale_log2 = scale * kLog2e;
-  CUtensorMap maps[4];
+  CUtensorMap maps[2];
   if (kv_maps) {
     maps[0] = kv_maps[0];
     maps[1] = kv_maps[1];
@@ -258,12 +250,10 @@ cudaError_t paged_decode_core(const bc_shape* s, const void* q, const void* k, c
       return cudaErrorInvalidValue;
     p.slot_major = sm ? 1 : 0;
   }
-  maps[2] = maps[0];
-  maps[3] = maps[1];
   const long long items = (long long)s->kv_heads * s->batch * p.row_chunks;
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   const int cluster = mode == kSplitCluster ? splits : 1;
-  cudaError_t e = launch_attn(s->dim, rt, false, out_half, p, maps, int(items), cluster, stream);
+  cudaError_t e = launch_attn(s->dim, rt, out_half, p, maps, int(items), cluster, stream);
   if (e != cudaSuccess || mode != kSplitGlobal || emit_partial) return e;
   const int rows = s->batch * s->query_heads;
   if (s->dim == 64)

@@ -1,0 +1,112 @@
+"""The multi-GPU host logic on CPU ranks (gloo, world size 2): request
+sharding covers every request once, and the split-KV exchange protocol of
+bc_dist (per-rank FP32 (m, l, acc) partials -> all-gather -> merge) gives the
+unsplit decode. The partials here come from a numpy restatement; on GPUs the
+same protocol runs with the CUDA entry points and NCCL."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from bc_dist import shard_pages, shard_requests, split_kv_decode
+
+
+def test_shard_requests_partition():
+    for batch in (1, 7, 8, 1024):
+        for world in (1, 2, 4, 8):
+            seen = []
+            for r in range(world):
+                seen += list(shard_requests(batch, world, r))
+            assert seen == list(range(batch))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _partial_numpy(q, k, v, pages, length, dim):
+    """(m, l, acc) of one request over its shard; m in natural-log units."""
+    hq, hkv = q.shape[0], k.shape[2]
+    g = hq // hkv
+    pml = np.zeros((hq, 2), np.float32)
+    pa = np.zeros((hq, dim), np.float32)
+    for h in range(hq):
+        toks = [k[pages[t // 16], t % 16, h // g] for t in range(length)]
+        vals = [v[pages[t // 16], t % 16, h // g] for t in range(length)]
+        if not toks:
+            pml[h] = (-np.inf, 0.0)
+            continue
+        s = np.stack(toks) @ q[h] / np.sqrt(dim)
+        m = s.max()
+        p = np.exp(s - m)
+        pml[h] = (m, p.sum())
+        pa[h] = p @ np.stack(vals)
+    return pml, pa
+
+
+def _merge_numpy(g_ml, g_a):
+    m = g_ml[..., 0].max(axis=0)
+    w = np.where(np.isfinite(g_ml[..., 0]), np.exp(g_ml[..., 0] - m), 0.0)
+    den = (w * g_ml[..., 1]).sum(axis=0)
+    return (w[..., None] * g_a).sum(axis=0) / den[:, None]
+
+
+def _worker(rank, world, port, data, result):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q, k, v, pages, length, dim = data
+        shard = shard_pages(len(pages), world, rank)
+        my_pages = pages[shard.start:shard.stop]
+        my_len = max(0, min(length - shard.start * 16, len(my_pages) * 16))
+
+        def local():
+            pml, pa = _partial_numpy(q, k, v, my_pages, my_len, dim)
+            return torch.from_numpy(pml), torch.from_numpy(pa)
+
+        def gather(t):
+            out = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(out, t)
+            return torch.stack(out)
+
+        def merge(g_ml, g_a):
+            return torch.from_numpy(_merge_numpy(g_ml.numpy(), g_a.numpy()).astype(np.float32))
+
+        out = split_kv_decode(local, merge, gather, q.shape[0], dim, world)
+        result[rank] = out.numpy()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+def test_split_kv_exchange_gloo_world2():
+    rng = np.random.default_rng(0)
+    hq, hkv, dim, length = 8, 2, 64, 300
+    npages = (length + 15) // 16
+    k = rng.standard_normal((npages + 3, 16, hkv, dim)).astype(np.float32)
+    v = rng.standard_normal((npages + 3, 16, hkv, dim)).astype(np.float32)
+    q = rng.standard_normal((hq, dim)).astype(np.float32)
+    pages = rng.permutation(npages + 3)[:npages]
+    full_ml, full_a = _partial_numpy(q, k, v, pages, length, dim)
+    expected = full_a / full_ml[:, 1:2]
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    result = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, (q, k, v, pages, length, dim), result))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(100)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert np.abs(result[r] - expected).max() < 1e-4
