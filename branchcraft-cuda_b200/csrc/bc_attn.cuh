@@ -170,26 +170,23 @@ __global__ void __launch_bounds__(kThreads, 2)
         int ids[kPagesPerStage];
 #pragma unroll
         for (int j = 0; j < kPagesPerStage; ++j) ids[j] = __shfl_sync(0xffffffffu, cur_ids, off + j);
-        if (lane == 0) {
-          uint8_t* st = smem + slot * STAGE;
-          mbar_arrive_expect_tx(&full[slot], uint32_t(np * 2 * PAGE));
-#pragma unroll
-          for (int j = 0; j < kPagesPerStage; ++j) {
-            if (j >= np) break;
-            const int v = v0 + j;
-            uint8_t* dk = st + j * 2 * PAGE;
-            uint8_t* dv = dk + PAGE;
-            if (v < npref) {
-              const int phys = ids[j];
-              // Out-of-pool ids read as zeros (TMA out-of-bounds fill).
-              if (phys < 0 || phys >= p.physical_pages) atomicOr(p.err, kErrPageRange);
-              const int c1 = p.slot_major ? 0 : kvh, c2 = p.slot_major ? kvh : 0;
-#pragma unroll
-              for (int kb = 0; kb < KB; ++kb) {
-                tma_load_4d(dk + kb * 2048, &kmap, &full[slot], kb * 64, c1, c2, phys);
-                tma_load_4d(dv + kb * 2048, &vmap, &full[slot], kb * 64, c1, c2, phys);
-              }
-            }
+        // Lane 0 posts the expected bytes; then each box of the stage is
+        // issued by its own lane (one issuing thread caps the copy rate).
+        uint8_t* st = smem + slot * STAGE;
+        if (lane == 0) mbar_arrive_expect_tx(&full[slot], uint32_t(np * 2 * PAGE));
+        __syncwarp();
+        if (lane < kPagesPerStage * KB * 2) {
+          const int j = lane / (KB * 2);
+          const int kb = (lane >> 1) % KB;
+          const bool is_v = lane & 1;
+          if (j < np) {
+            const int phys = ids[j];
+            // Out-of-pool ids read as zeros (TMA out-of-bounds fill).
+            if (!is_v && kb == 0 && (phys < 0 || phys >= p.physical_pages))
+              atomicOr(p.err, kErrPageRange);
+            const int c1 = p.slot_major ? 0 : kvh, c2 = p.slot_major ? kvh : 0;
+            uint8_t* dst = st + j * 2 * PAGE + (is_v ? PAGE : 0) + kb * 2048;
+            tma_load_4d(dst, is_v ? &vmap : &kmap, &full[slot], kb * 64, c1, c2, phys);
           }
         }
         __syncwarp();

@@ -16,11 +16,14 @@
 // output uses P = hi + lo and two MMAs) to shared memory, O += P V (UMMA
 // 128xDx16, V as an MN-major operand) accumulating in TMEM.
 //
-// Warp roles (192 threads): warps 0-3 softmax + epilogue (thread t owns row t
-// = TMEM lane t), warp 4 TMA producer (K/V pages of the page table, draft
-// K/V), warp 5 TMEM allocator and single-thread MMA issuer. K/V tiles stream
-// through a 3-stage ring; S and P are double-buffered so the softmax of tile i
-// overlaps S of tile i+1 and PV of tile i-1.
+// Warp roles (320 threads): two softmax warpgroups (warps 0-3 and 4-7) take
+// alternate key tiles, each with its own online-softmax state and its own O
+// accumulator in TMEM (thread (w & 3)*32 + lane owns row = TMEM lane of that
+// index); they are merged in the epilogue. Warp 8 is the TMA producer (K/V
+// pages of the page table, draft K/V), warp 9 the TMEM allocator and the
+// single-thread MMA issuer. K/V tiles stream through a 3-stage ring; S/P
+// buffer g belongs to group g, so both groups' softmax overlap each other and
+// the MMAs of their neighbouring tiles.
 //
 // The running max is kept lazily: O and l are rescaled only when a row's max
 // grows by more than 2^8 (rare after the first tile), with probabilities up
@@ -37,7 +40,7 @@ namespace bc {
 constexpr int kTreeRows = 128;
 constexpr int kTreeTile = 64;        // keys per tile = 4 pages
 constexpr int kTreeStages = 3;
-constexpr int kTreeThreads = 192;
+constexpr int kTreeThreads = 320;   // 8 softmax warps, producer, MMA issuer
 constexpr int kTreeMaxReq = 128;     // requests per CTA (rows per request >= 1)
 
 struct TreeParams {
@@ -73,14 +76,15 @@ struct TreeGeom {
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   // misc: tmem base (4) + nruns (4) + run tables 6 x kTreeMaxReq ints
   static constexpr int kRunOff = kMiscOff + 16;
-  static constexpr int kParOff = kRunOff + 6 * kTreeMaxReq * 4;
+  static constexpr int kWg1Off = kRunOff + 6 * kTreeMaxReq * 4;  // [128][2] second group's (m, l)
+  static constexpr int kParOff = kWg1Off + kTreeRows * 8;
   static constexpr int kOStride = D + 4;
   static_assert(kTreeRows * kOStride * 4 + kTreeRows * 8 <= kTreeStages * kStageBytes,
                 "epilogue buffers must fit in the K/V ring");
   // parent rows (anc_rows ints, 16-byte padded) then ancestor sets (32 B each)
   __host__ __device__ static size_t anc_offset(int anc_rows) { return size_t(kParOff) + ((size_t(anc_rows) * 4 + 15) & ~size_t(15)); }
   static size_t smem_bytes(int anc_rows) { return 1024 + anc_offset(anc_rows) + size_t(anc_rows) * 32; }
-  static constexpr uint32_t kTmemCols = 256;  // S: 2 x 64, O: D (<= 128)
+  static constexpr uint32_t kTmemCols = 512;  // S/P: 2 x 64, O: 2 x D (<= 128 each)
 };
 
 template <int D, bool PREC, bool OUT_HALF>
@@ -152,7 +156,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     mbar_init(mma_done, 1);
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, G::kTmemCols);
     tmem_relinquish();
   }
@@ -219,7 +223,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // Producer: speculative page ids of tiles 0..15 of this CTA's range under
   // the assumption that all requests of the block share request b0's prefix.
   int spec_len0 = 0, spec_v0 = 0, cur_ids = -1, next_ids = -1;
-  if (warp == 4) {
+  if (warp == 8) {
     spec_len0 = min(max(__ldg(p.lengths + b0), 0), cap);
     const int t0 = (spec_len0 + kTreeTile - 1) / kTreeTile;
     const int tot = t0 + ndraft_tiles;
@@ -302,7 +306,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   const uint32_t kv_addr = smem_u32(smem + G::kKVOff);
   const uint32_t p_addr = smem_u32(smem + G::kPOff);
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (ntiles > 0) {
       int run, t;
@@ -349,27 +353,24 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             if (ids[j] >= p.physical_pages || ids[j] < -1) atomicOr(p.err, kErrPageRange);
-        if (lane == 0) {
-          uint8_t* kdst = smem + G::kKVOff + stage * G::kStageBytes;
-          uint8_t* vdst = kdst + G::kHalfTile;
-          mbar_arrive_expect_tx(&kv_full[stage], uint32_t(G::kStageBytes));
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-#pragma unroll
-            for (int kb = 0; kb < KB; ++kb) {
-              uint8_t* kd = kdst + kb * (kTreeTile * 128) + j * 2048;
-              uint8_t* vd = vdst + kb * (kTreeTile * 128) + j * 2048;
-              if (is_prefix) {
-                tma_load_4d(kd, &kmap, &kv_full[stage], kb * 64, kvh, 0, ids[j]);
-                tma_load_4d(vd, &vmap, &kv_full[stage], kb * 64, kvh, 0, ids[j]);
-              } else {
-                const int slot = (t * 4 + j) * 16;  // draft slot of this box
-                const int rq = slot / npad, nb = slot % npad;
-                const int b = rq < nreq ? b0 + rq : p.batch;  // past the block: zeros
-                tma_load_4d(kd, &dkmap, &kv_full[stage], kb * 64, kvh, nb, b);
-                tma_load_4d(vd, &dvmap, &kv_full[stage], kb * 64, kvh, nb, b);
-              }
-            }
+        // Lane 0 posts the expected bytes, then every box of the tile is
+        // issued by its own lane: a single issuing thread caps the copy rate
+        // of the CTA well below what the tensor cores consume.
+        uint8_t* kdst = smem + G::kKVOff + stage * G::kStageBytes;
+        if (lane == 0) mbar_arrive_expect_tx(&kv_full[stage], uint32_t(G::kStageBytes));
+        __syncwarp();
+        if (lane < 4 * KB * 2) {
+          const int j = lane / (KB * 2);         // page of the tile
+          const int kb = (lane >> 1) % KB;       // 64-dim half
+          const bool is_v = lane & 1;
+          uint8_t* dst = kdst + (is_v ? G::kHalfTile : 0) + kb * (kTreeTile * 128) + j * 2048;
+          if (is_prefix) {
+            tma_load_4d(dst, is_v ? &vmap : &kmap, &kv_full[stage], kb * 64, kvh, 0, ids[j]);
+          } else {
+            const int slot = (t * 4 + j) * 16;  // draft slot of this box
+            const int rq = slot / npad, nb = slot % npad;
+            const int b = rq < nreq ? b0 + rq : p.batch;  // past the block: zeros
+            tma_load_4d(dst, is_v ? &dvmap : &dkmap, &kv_full[stage], kb * 64, kvh, nb, b);
           }
         }
         __syncwarp();
@@ -380,12 +381,11 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (ntiles > 0 && lane == 0) {
       bool ok = true;
       const uint32_t tS[2] = {tbase, tbase + 64};
-      const uint32_t tO = tbase + 128;
       auto issue_pv = [&](int i) {
         const int stage = i % kTreeStages;
         const int buf = i & 1;
@@ -393,13 +393,14 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         tc_fence_after();
         const uint32_t vbase = kv_addr + stage * G::kStageBytes + G::kHalfTile;
         const uint32_t pbase = p_addr + buf * G::kPBufBytes;
+        const uint32_t tO = tbase + 128 + buf * 128;  // group buf's accumulator
 #pragma unroll
         for (int kk = 0; kk < kTreeTile / 16; ++kk) {
           // V: MN-major (dims contiguous); 16 keys = two 8-key groups 1024 B apart;
           // the second 64-dim block sits kTreeTile*128 bytes further.
           const uint64_t bdesc = umma_desc_sw128(vbase + kk * 2048, kTreeTile * 128, 1024);
           const uint64_t adesc = umma_desc_sw128(pbase + kk * 32, 16, 1024);
-          umma_f16(tO, adesc, bdesc, kIdescPV, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_f16(tO, adesc, bdesc, kIdescPV, (i >= 2 || kk > 0) ? 1u : 0u);
           if (PREC) {
             const uint64_t ldesc = umma_desc_sw128(pbase + G::kPBytes + kk * 32, 16, 1024);
             umma_f16(tO, ldesc, bdesc, kIdescPV, 1u);
@@ -436,18 +437,20 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
 
   // ------------------------------------------------------------ softmax rows
   float m_ref = kNegInf, l_sum = 0.f;
-  const int r = tid;  // row of the tile (warps 0-3)
+  const int wg = warp >> 2;                 // softmax group (warps 0-7)
+  const int r = (warp & 3) * 32 + lane;     // row of the tile = TMEM lane
   const int brow = trow * kTreeRows + r;
-  const bool row_valid = warp < 4 && brow < nreq * p.rows_req;
+  const bool row_valid = warp < 8 && brow < nreq * p.rows_req;
   const int my_req = row_valid ? brow / p.rows_req : -1;
   const int my_node = row_valid ? (brow % p.rows_req) / p.group : 0;
-  const uint32_t lane_addr = uint32_t(warp * 32) << 16;
+  const uint32_t lane_addr = uint32_t((warp & 3) * 32) << 16;
+  const uint32_t o_col = 128 + uint32_t(wg & 1) * 128;  // this group's O in TMEM
   bool softmax_ok = true;
-  if (warp < 4 && ntiles > 0) {
+  if (warp < 8 && ntiles > wg) {
     int run, t;
-    start_cursor(v0, run, t);
+    start_cursor(v0 + wg, run, t);
     const uint32_t* my_anc = anc + (size_t(max(my_req, 0)) * p.nodes + my_node) * 8;
-    for (int i = 0; i < ntiles; ++i) {
+    for (int i = wg; i < ntiles; i += 2) {
       const int buf = i & 1;
       if (!mbar_wait(&s_full[buf], (i >> 1) & 1)) {
         softmax_ok = false;
@@ -471,13 +474,16 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         valid_keys = min(kTreeTile, run_len[run] - t * kTreeTile);
         in_run = row_valid && my_req >= run_first[run] && my_req < run_end[run];
       }
+      // x[c] holds the raw score (masked keys: -inf); the scale (> 0) is
+      // applied after the max and inside the exponent's FMA.
       float x[64];
-      if (is_prefix) {
+      if (is_prefix && in_run && valid_keys == kTreeTile) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const bool ok = in_run && c < valid_keys;
-          x[c] = ok ? __uint_as_float(s[c]) * p.scale_log2 : kNegInf;
-        }
+        for (int c = 0; c < 64; ++c) x[c] = __uint_as_float(s[c]);  // full tile: no mask
+      } else if (is_prefix) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          x[c] = (in_run && c < valid_keys) ? __uint_as_float(s[c]) : kNegInf;
       } else {
         const int slot0 = t * kTreeTile;
 #pragma unroll
@@ -488,7 +494,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           if (row_valid && rq == my_req) bits = (my_anc[nb >> 5] >> (nb & 31)) & 0xffffu;
 #pragma unroll
           for (int e = 0; e < 16; ++e)
-            x[c + e] = ((bits >> e) & 1u) ? __uint_as_float(s[c + e]) * p.scale_log2 : kNegInf;
+            x[c + e] = ((bits >> e) & 1u) ? __uint_as_float(s[c + e]) : kNegInf;
         }
       }
       float mx;
@@ -500,6 +506,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         for (int c = 8; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], x[c]);
         mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                    fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        mx *= p.scale_log2;  // -inf stays -inf
       }
       // Lazy max: move the reference only when the max grows by > 8 (log2).
       float alpha = 1.f;
@@ -523,7 +530,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         uint32_t hi[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
-          const float p0 = fast_exp2(x[c + e] - mb), p1 = fast_exp2(x[c + e + 1] - mb);
+          const float p0 = fast_exp2(fmaf(x[c + e], p.scale_log2, -mb));
+          const float p1 = fast_exp2(fmaf(x[c + e + 1], p.scale_log2, -mb));
           ls[(e >> 1) & 3] += p0 + p1;
           if (PREC) {
             // Veltkamp split: h = p rounded to 11 significant bits (exact in
@@ -559,30 +567,26 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         }
       }
       fence_proxy_async_smem();
-      // O rescale (whole warp when any of its rows needs it): O must include
-      // PV of tile i-1 first.
+      // O rescale (whole warp when any of its rows needs it). This group's
+      // previous PV (tile i-2) is complete: it was waited for above.
       if (__any_sync(0xffffffffu, rescale)) {
-        if (i >= 1 && !mbar_wait(&pv_done[(i - 1) & 1], ((i - 1) >> 1) & 1)) {
-          softmax_ok = false;
-          break;
-        }
         tc_fence_after();
         const float f = rescale ? alpha : 1.f;
 #pragma unroll
         for (int c = 0; c < D; c += 32) {
           uint32_t o[32];
-          tmem_ld32(tbase + lane_addr + 128 + c, o);
+          tmem_ld32(tbase + lane_addr + o_col + c, o);
           tmem_ld_wait();
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-          tmem_st32(tbase + lane_addr + 128 + c, o);
+          tmem_st32(tbase + lane_addr + o_col + c, o);
         }
         tmem_st_wait();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[buf]);
-      ++t;
+      t += 2;  // the other group takes the tile in between
       while (run < nruns && t >= run_tiles[run]) {  // empty runs have no tiles
         t -= run_tiles[run];
         ++run;
@@ -602,24 +606,48 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     const int rq = br / p.rows_req, node = (br % p.rows_req) / p.group, hh = br % p.group;
     return ((size_t(b0 + rq) * p.nodes + node) * p.hq + size_t(kvh) * p.group + hh) * D;
   };
-  if (warp < 4) {
-    const int last = ntiles - 1;
-    bool have = ntiles > 0 && softmax_ok;
+  // Group 1 hands its (m, l) to group 0 through shared memory; group 0 merges
+  // the two O accumulators row by row.
+  float* wg1_ml = reinterpret_cast<float*>(smem + G::kWg1Off);
+  bool have = false;
+  if (warp < 8) {
+    have = ntiles > wg && softmax_ok;
+    const int last = have ? wg + 2 * ((ntiles - 1 - wg) / 2) : 0;
     if (have && !mbar_wait(&pv_done[last & 1], (last >> 1) & 1)) {
       have = false;
       if (lane == 0) atomicOr(p.err, kErrTimeout);
     }
+    if (wg == 1) {
+      wg1_ml[r * 2 + 0] = have ? m_ref : kNegInf;
+      wg1_ml[r * 2 + 1] = have ? l_sum : 0.f;
+    }
+    named_barrier_sync(2, 256);
+  }
+  if (warp < 4) {
     tc_fence_after();
-    const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+    const float m1 = wg1_ml[r * 2 + 0], l1 = wg1_ml[r * 2 + 1];
+    const float m0 = have ? m_ref : kNegInf, l0 = have ? l_sum : 0.f;
+    const float mm = fmaxf(m0, m1);
+    // Per row: a group contributes only if its max is finite. The TMEM reads
+    // themselves are warp-collective, so they depend only on whether the
+    // group processed any tile at all (uniform across the warp).
+    const bool use0 = m0 != kNegInf, use1 = m1 != kNegInf;
+    const float w0 = use0 ? fast_exp2(m0 - mm) : 0.f;
+    const float w1 = use1 ? fast_exp2(m1 - mm) : 0.f;
+    const float lsum = w0 * l0 + w1 * l1;
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    const bool read0 = ntiles > 0, read1 = ntiles > 1;
 #pragma unroll 1
     for (int c = 0; c < D; c += 32) {
-      uint32_t o[32];
-      if (have) {
-        tmem_ld32(tbase + lane_addr + 128 + c, o);
-        tmem_ld_wait();
-      } else {
+      uint32_t o[32], o1[32];
+      if (read0) tmem_ld32(tbase + lane_addr + 128 + c, o);
+      if (read1) tmem_ld32(tbase + lane_addr + 256 + c, o1);
+      tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = 0u;
+      for (int e = 0; e < 32; ++e) {
+        const float a = (read0 && use0) ? w0 * __uint_as_float(o[e]) : 0.f;
+        const float b = (read1 && use1) ? w1 * __uint_as_float(o1[e]) : 0.f;
+        o[e] = __float_as_uint(a + b);
       }
       if (to_cluster) {
 #pragma unroll
@@ -651,13 +679,13 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       }
     }
     if (to_cluster) {
-      fml[r * 2 + 0] = have ? m_ref : kNegInf;
-      fml[r * 2 + 1] = have ? l_sum : 0.f;
+      fml[r * 2 + 0] = mm;
+      fml[r * 2 + 1] = lsum;
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tbase, G::kTmemCols);
   }
