@@ -29,7 +29,7 @@ EXPORTS = (
     "bc_decode", "bc_auto_splits", "bc_paged_decode", "bc_paged_decode_partial",
     "bc_tree_verify", "bc_tree_verify_f16", "bc_commit_path", "bc_commit_batch",
     "bc_packed_decode", "bc_packed_decode_kv", "bc_merge_partials",
-    "bc_last_device_error", "bc_version",
+    "bc_last_device_error", "bc_version", "bc_decode_static_scratch",
 )
 
 
@@ -60,6 +60,7 @@ _sigs = {
     "bc_packed_decode": [_SP, _vp, _vp, _vp, _vp, _vp, _ll, _ll, _ll, _f, _vp],
     "bc_packed_decode_kv": [_SP, _vp, _vp, _vp, _vp, _vp, _ll, _ll, _ll, _ll, _f, _i, _vp],
     "bc_merge_partials": [_i, _i, _i, _vp, _vp, _vp, _vp],
+    "bc_decode_static_scratch": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "bc_last_device_error": [_i],
     "bc_version": [],
 }
@@ -173,6 +174,18 @@ def merge_partials(partial_ml, partial_a, out, stream=None):
     splits, rows, dim = partial_a.shape
     _check(_lib.bc_merge_partials(splits, rows, dim, _ptr(partial_ml), _ptr(partial_a),
                                   _ptr(out), _stream(stream)), "bc_merge_partials")
+
+
+def decode_static_scratch(shape: Shape, q, k, v, pages, lengths, output, splits=1,
+                          stream=None, check=True):
+    """bc_decode with the split partials in the library's fixed device array
+    (no caller scratch, nothing allocated)."""
+    rc = _lib.bc_decode_static_scratch(ctypes.byref(shape), _ptr(q), _ptr(k), _ptr(v),
+                                       _ptr(pages), _ptr(lengths), _ptr(output), splits,
+                                       _stream(stream))
+    if check:
+        _check(rc, "bc_decode_static_scratch")
+    return rc
 
 
 def last_device_error(reset: bool = True) -> int:

@@ -610,6 +610,59 @@ int bc_merge_partials(int splits, int rows, int dim, const float* partial_ml,
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free decode: split partials in a library-owned device array.
+// ---------------------------------------------------------------------------
+}  // extern "C"
+
+namespace {
+
+// The array is a device symbol: host code must use its device address, which
+// cudaGetSymbolAddress returns for the device that is current at the call.
+static __device__ __align__(256) float bc_static_decode_scratch[BC_STATIC_SCRATCH_FLOATS];
+
+float* static_scratch_address(int dev) {
+  static std::atomic<float*> cache[kMaxDevices];
+  static std::mutex mu;
+  float* p = cache[dev].load(std::memory_order_acquire);
+  if (p) return p;
+  std::lock_guard<std::mutex> lock(mu);
+  p = cache[dev].load(std::memory_order_relaxed);
+  if (!p) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, bc_static_decode_scratch) != cudaSuccess || !addr)
+      return nullptr;
+    p = static_cast<float*>(addr);
+    cache[dev].store(p, std::memory_order_release);
+  }
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bc_decode_static_scratch(const bc_shape* s, const void* q, const void* k, const void* v,
+                             const int* pages, const int* lengths, float* output, int splits,
+                             void* stream) {
+  if (!basic_shape_ok(s) || splits < 1 || splits > BC_MAX_SPLITS || !q || !k || !v || !pages ||
+      !lengths || !output)
+    return cudaErrorInvalidValue;
+  const long long rows = (long long)s->batch * s->query_heads;
+  const long long need = (long long)splits * rows * (s->dim + 2);
+  if (need > BC_STATIC_SCRATCH_FLOATS) return cudaErrorInvalidValue;  // beyond the fixed array
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  float* scratch = static_scratch_address(dev);
+  if (!scratch) return cudaErrorInvalidDevice;
+  float* partial_a = scratch;                                  // splits * rows * dim
+  float* partial_ml = scratch + (long long)splits * rows * s->dim;  // splits * rows * 2
+  return paged_decode_core(s, q, k, v, pages, lengths, output, false,
+                           1.0f / std::sqrt(float(s->dim)), splits,
+                           splits > 1 ? kSplitGlobal : kSplitNone, false, partial_a, partial_ml,
+                           false, nullptr, static_cast<cudaStream_t>(stream));
+}
+
 unsigned bc_last_device_error(int reset) {
   const int dev = current_device();
   if (dev < 0) return 0xffffffffu;

@@ -157,6 +157,27 @@ int bc_paged_decode_partial(const bc_shape* shape, const void* q, const void* k,
                             const void* v, const int* pages, const int* lengths,
                             float* partial_ml, float* partial_a, int splits, void* stream);
 
+/* Paged split-KV decode, as bc_decode, for callers that cannot allocate device
+ * memory: an attention plugin handed only its input and output buffers by an
+ * engine that owns every allocation, or a latency-critical decode loop whose
+ * memory plan forbids allocating per step (cudaMalloc may synchronise the
+ * device and fragments the pool). Instead of caller scratch, the split
+ * partials live in a fixed device array inside this library: at most
+ * BC_STATIC_SCRATCH_FLOATS floats, i.e. splits * batch * query_heads *
+ * (dim + 2) <= 2,097,152 (8 MiB on every GPU that loads the library, held
+ * until the process exits). Larger requests return cudaErrorInvalidValue.
+ * splits in [1, BC_MAX_SPLITS]; splits > 1 always merges through that array.
+ * The first call on a device looks up the array's device address (with that
+ * device current); make that first call before any stream capture. All calls
+ * share the one array: calls that overlap on the GPU (other streams, other
+ * threads) race and must be serialised by the caller. Every call rewrites all
+ * the partials it reads, so nothing has to be cleared between calls.
+ * No counterpart in the reference. */
+#define BC_STATIC_SCRATCH_FLOATS (1 << 21)
+int bc_decode_static_scratch(const bc_shape* shape, const void* q, const void* k,
+                             const void* v, const int* pages, const int* lengths,
+                             float* output, int splits, void* stream);
+
 /* Returns the current device's error word (BC_ERR_* bits; 0 = clean) after
  * synchronising that device; reset != 0 clears it. */
 unsigned bc_last_device_error(int reset);
