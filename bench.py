@@ -1,29 +1,41 @@
 """Benchmark of the branchcraft B200 hot path.
 
-Default workload (the configuration the headline metric is
-quoted on): one speculative-verification step for a batch of 8 requests that
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload tree-cow|tree-oracle|decode|packed|tree-scale|longctx]
+
+Default workload `tree-cow` (the configuration the headline
+metric is quoted on): one speculative-verification step for 8 requests that
 share a 2040-token paged prefix — `tree_verify` over every request's 7-node
 draft tree, then the copy-on-write commit of every request's accepted path
 (7 shared-page clones + the path rows) — Hq=32, Hkv=8, D=128, FP16 inputs,
-FP32 accumulation and output.
+FP32 accumulation and output. `value` is the whole-job algorithmic HBM
+traffic rate (all ranks' bytes / max-over-ranks device time, TB/s);
+`ms_per_step` is the verify+commit step time.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+The other workloads are the remaining BASELINE configurations (one line each,
+for the design notes; the driver runs the default):
+  tree-oracle  config 1: 1 request, 2048-token prefix, 7 nodes, FP16 output
+  decode       config 3: paged split-KV decode, B x context (default 4 x 131072)
+  packed       config 4: vLLM-layout packed decode, B=256, lengths U[512, 8192]
+  tree-scale   config 5a: 1024 requests x 63-node trees, 4096-token prefix per 16
+               (strong scaling: the requests are split across ranks)
+  longctx      config 5b: one 1,048,576-token context split across ranks; per-rank
+               FP32 partials all-gathered over NCCL and merged on the device
 
-One process per GPU (torchrun for N > 1). Every rank runs its own batch
-(weak scaling, no data-path collective: requests are independent); `value` is
-the whole-job algorithmic HBM traffic rate (all ranks' bytes / max-over-ranks
-device time). The inputs (~10 MB) fit in L2, so L2 is flushed (a 256 MiB
-device write) between timed steps, outside the per-step CUDA events.
+One process per GPU (torchrun for N > 1). Request-sharded workloads run every
+rank on its own batch (weak scaling, no data-path collective). Inputs smaller
+than L2 (tree-cow, tree-oracle) are followed by an L2 flush (a 256 MiB device
+write) outside each step's CUDA events; the others stream more than L2.
 
-`--impl reference` times the reference's own CPU implementation of the step
-(its CPU oracle `cpu_tree_reference`, src/main.cu:204-240, compiled unmodified
-from the reference sources into oracle/_ref/libbcref.so, run on one request per
-host thread, plus the numpy page copies of the commit) on rank 0 only.
+`--impl reference` times the reference's own CPU implementation on rank 0 (its
+CPU oracle, compiled unmodified from src/main.cu into oracle/_ref/libbcref.so,
+one request per host thread), on the same inputs and in the same unit.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -39,8 +51,8 @@ sys.path.insert(0, str(ROOT / "branchcraft-cuda_b200"))
 
 METRIC = "tree_verify µs & HBM TB/s per B200; decode tokens/s at 1/2/4/8 GPUs"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
-FALLBACK_HBM_GBS = 6650.0
 FLUSH_BYTES = 256 << 20
+SCALE = 1.0 / math.sqrt(128.0)
 
 
 def load_peaks():
@@ -48,13 +60,13 @@ def load_peaks():
         p = json.loads(PEAKS.read_text())
         return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
     except Exception:
-        return FALLBACK_HBM_GBS, 1590.0, "fallback"
+        return 6650.0, 1590.0, "fallback"
 
 
 # --------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 100 ms in the
-    background; `window(t0, t1)` summarises the samples inside [t0, t1]."""
+    """nvidia-smi clocks / throttle reasons every 100 ms in the background;
+    `window(t0, t1)` summarises the samples inside [t0, t1]."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -68,8 +80,7 @@ class ClockSampler:
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100", "-i", str(device_index)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
+            threading.Thread(target=self._read, daemon=True).start()
         except Exception:
             self.proc = None
 
@@ -114,10 +125,8 @@ class ClockSampler:
 
 # --------------------------------------------------------------- helpers
 def dist_env():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    return (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")),
+            int(os.environ.get("LOCAL_RANK", "0")))
 
 
 def to_dev(torch, a, device):
@@ -129,11 +138,606 @@ def to_dev(torch, a, device):
 
 def pinned(torch, a):
     a = np.ascontiguousarray(a)
-    if a.dtype == np.uint16:
-        t = torch.from_numpy(a.view(np.int16).copy()).view(torch.float16)
-    else:
-        t = torch.from_numpy(a.copy())
+    t = (torch.from_numpy(a.view(np.int16).copy()).view(torch.float16) if a.dtype == np.uint16
+         else torch.from_numpy(a.copy()))
     return t.pin_memory()
+
+
+def half_bits(torch, t):
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def oracle_module():
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+
+    return O
+
+
+class Events:
+    """Pairs of CUDA events recorded on a stream; `ms()` their durations."""
+
+    def __init__(self, torch, n):
+        self.ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(n)]
+
+    def ms(self):
+        return [a.elapsed_time(b) for a, b in self.ev]
+
+
+# --------------------------------------------------------------- workloads
+# Each workload: setup(), device_step(i, kev), e2e_step(), and facts for the
+# JSON line. `kev` is a pair of events bracketing the dominant kernel.
+
+class TreeCow:
+    name = "tree-cow"
+    flush = True
+    higher_is_better = True
+    unit = "TB/s"
+
+    def __init__(self, torch, C, device, rank, world, **_):
+        from bc_workloads import TreeCowWorkload
+
+        self.torch, self.C, self.device = torch, C, device
+        wl = self.wl = TreeCowWorkload(seed=2040 + rank)
+        self.plan, _ = wl.plan()
+        self.shape = C.make_shape(*wl.shape())
+        k0, v0 = wl.initial_cache()
+        self.ck, self.cv = to_dev(torch, k0, device), to_dev(torch, v0, device)
+        plan = self.plan
+        self.host = {
+            "draft_q": pinned(torch, wl.draft_q), "draft_k": pinned(torch, wl.draft_k),
+            "draft_v": pinned(torch, wl.draft_v), "parent": pinned(torch, wl.parent),
+            "pages": pinned(torch, wl.pages), "lengths": pinned(torch, wl.lengths),
+            "clone_src": pinned(torch, np.array(plan.clone_src, np.int32)),
+            "clone_dst": pinned(torch, np.array(plan.clone_dst, np.int32)),
+            "e_req": pinned(torch, np.array(plan.entry_request, np.int32)),
+            "e_node": pinned(torch, np.array(plan.entry_node, np.int32)),
+            "e_page": pinned(torch, np.array(plan.entry_page, np.int32)),
+            "e_slot": pinned(torch, np.array(plan.entry_slot, np.int32)),
+        }
+        self.dev = {n: t.to(device) for n, t in self.host.items()}
+        self.out = torch.empty(wl.batch, wl.nodes, wl.hq, wl.dim, device=device)
+        self.out_host = torch.empty(self.out.shape, dtype=torch.float32).pin_memory()
+        self.launches = 1 + bool(plan.clone_src) + bool(plan.entry_node)
+        self.step_bytes = wl.verify_bytes() + wl.commit_bytes(plan)
+        self.kernel_bytes = wl.verify_bytes()
+        self.kernel = "tree_mma_kernel (tree_verify)"
+        self.bound = "hbm"
+
+    def device_step(self, kev=None):
+        d, C, wl = self.dev, self.C, self.wl
+        if kev:
+            kev[0].record()
+        C.tree_verify(self.shape, d["draft_q"], self.ck, self.cv, d["pages"], d["lengths"],
+                      d["draft_k"], d["draft_v"], d["parent"], self.out, wl.nodes)
+        if kev:
+            kev[1].record()
+        C.commit_batch(self.shape, wl.nodes, d["draft_k"], d["draft_v"], self.ck, self.cv,
+                       d["clone_src"], d["clone_dst"], d["e_req"], d["e_node"], d["e_page"],
+                       d["e_slot"])
+
+    def e2e_step(self):
+        for n, t in self.host.items():
+            self.dev[n].copy_(t, non_blocking=True)
+        self.device_step()
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    def io_bytes(self):
+        return (sum(t.numel() * t.element_size() for t in self.host.values()),
+                self.out_host.numel() * 4)
+
+    def value(self, steps_all_ranks, seconds):
+        return self.step_bytes * steps_all_ranks / seconds / 1e12
+
+    def config(self):
+        wl = self.wl
+        return {"workload": "BASELINE config 2: batched shared-prefix tree_verify + COW "
+                            "commit_path_ (8 requests, shared 2040-token prefix, 7-node random "
+                            "trees, Hq=32 Hkv=8 D=128, page 16)",
+                "requests_per_gpu": wl.batch, "prefix_tokens": wl.prefix,
+                "tree_nodes": wl.nodes, "step_bytes": self.step_bytes,
+                "verify_bytes_per_launch": wl.verify_bytes(),
+                "verify_flops_per_launch": wl.verify_flops(),
+                "commit_clones": len(self.plan.clone_src),
+                "commit_rows": len(self.plan.entry_node)}
+
+    def cpu_baseline(self):
+        """The oracle port (OpenMP over rows) on one full step."""
+        O = oracle_module()
+        from cow_oracle import CowOracle
+
+        wl = self.wl
+        k0, v0 = wl.initial_cache()
+        t = time.perf_counter()
+        O.tree(wl.shape(), wl.nodes, wl.draft_q, k0, v0, wl.pages, wl.lengths, wl.draft_k,
+               wl.draft_v, wl.parent, threads=O.max_threads())
+        cow = CowOracle(wl.pool_pages, wl.hkv, wl.dim)
+        r0 = cow.new(wl.prefix_k, wl.prefix_v)
+        reqs = [r0] + [cow.fork(r0) for _ in range(wl.batch - 1)]
+        for b in range(wl.batch):
+            cow.commit(reqs[b], wl.paths[b], wl.draft_k[b], wl.draft_v[b])
+        dt = time.perf_counter() - t
+        return {"value": self.step_bytes / dt / 1e12, "unit": self.unit,
+                "cores": O.max_threads(), "kind": "port",
+                "sample": "1 full step (8-request tree verify + 8 COW commits)",
+                "seconds": round(dt, 4)}
+
+    def reference_step(self, pool):
+        """The reference's cpu_tree_reference per request (one per thread) +
+        the sequential COW commits; returns (seconds, bytes)."""
+        O = oracle_module()
+        from cow_oracle import CowOracle
+
+        wl = self.wl
+        k0, v0 = wl.initial_cache()
+
+        def one(b):
+            s = (1, wl.hq, wl.hkv, wl.dim, wl.max_pages, wl.pool_pages)
+            return O.ref_cpu_tree_reference(s, wl.nodes, wl.draft_q[b:b + 1], k0, v0,
+                                            wl.pages[b:b + 1], wl.lengths[b:b + 1],
+                                            wl.draft_k[b:b + 1], wl.draft_v[b:b + 1],
+                                            wl.parent[b:b + 1])
+
+        t = time.perf_counter()
+        list(pool.map(one, range(wl.batch)))
+        cow = CowOracle(wl.pool_pages, wl.hkv, wl.dim)
+        r0 = cow.new(wl.prefix_k, wl.prefix_v)
+        reqs = [r0] + [cow.fork(r0) for _ in range(wl.batch - 1)]
+        for b in range(wl.batch):
+            cow.commit(reqs[b], wl.paths[b], wl.draft_k[b], wl.draft_v[b])
+        return time.perf_counter() - t, self.step_bytes, wl.batch
+
+
+class TreeOracle(TreeCow):
+    """one request, 2048-token prefix in a seeded permutation
+    of a 256-page pool, parents [-1,0,0,1,1,2,2], FP16 output."""
+
+    name = "tree-oracle"
+
+    def __init__(self, torch, C, device, rank, world, **_):
+        self.torch, self.C, self.device = torch, C, device
+        rng = np.random.default_rng(2048 + rank)
+        from bc_workloads import rand_half
+
+        P, prefix, N = 256, 2048, 7
+        self.N, self.prefix = N, prefix
+        self.k = rand_half(rng, (P, 16, 8, 128))
+        self.v = rand_half(rng, (P, 16, 8, 128))
+        self.pages = rng.permutation(P).astype(np.int32)[:prefix // 16].reshape(1, -1)
+        self.lengths = np.array([prefix], np.int32)
+        self.dq = rand_half(rng, (1, N, 32, 128))
+        self.dk = rand_half(rng, (1, N, 8, 128))
+        self.dv = rand_half(rng, (1, N, 8, 128))
+        self.parent = np.array([[-1, 0, 0, 1, 1, 2, 2]], np.int32)
+        self.shape = C.make_shape(1, 32, 8, 128, prefix // 16, P)
+        self.ck, self.cv = to_dev(torch, self.k, device), to_dev(torch, self.v, device)
+        self.host = {"dq": pinned(torch, self.dq), "dk": pinned(torch, self.dk),
+                     "dv": pinned(torch, self.dv), "parent": pinned(torch, self.parent),
+                     "pages": pinned(torch, self.pages), "lengths": pinned(torch, self.lengths)}
+        self.dev = {n: t.to(device) for n, t in self.host.items()}
+        self.out = torch.empty(1, N, 32, 128, device=device, dtype=torch.float16)
+        self.out_host = torch.empty(self.out.shape, dtype=torch.float16).pin_memory()
+        self.launches = 1
+        self.step_bytes = (prefix * 4096 + N * 8 * 128 * 2 * 2 + N * 32 * 128 * 2
+                           + N * 32 * 128 * 2 + prefix // 16 * 4 + 4 + N * 4)
+        self.kernel_bytes = self.step_bytes
+        self.kernel = "tree_mma_kernel (tree_verify, FP16 out)"
+        self.bound = "hbm"
+
+    def device_step(self, kev=None):
+        d = self.dev
+        if kev:
+            kev[0].record()
+        self.C.tree_verify(self.shape, d["dq"], self.ck, self.cv, d["pages"], d["lengths"],
+                           d["dk"], d["dv"], d["parent"], self.out, self.N)
+        if kev:
+            kev[1].record()
+
+    def io_bytes(self):
+        return (sum(t.numel() * t.element_size() for t in self.host.values()),
+                self.out_host.numel() * 2)
+
+    def config(self):
+        return {"workload": "BASELINE config 1: tree_verify, 1 request, 2048-token prefix in a "
+                            "permuted 256-page pool, parents [-1,0,0,1,1,2,2], FP16 output",
+                "step_bytes": self.step_bytes}
+
+    def cpu_baseline(self):
+        O = oracle_module()
+        t = time.perf_counter()
+        O.tree(self.shape_tuple(), self.N, self.dq, self.k, self.v, self.pages, self.lengths,
+               self.dk, self.dv, self.parent, threads=O.max_threads())
+        dt = time.perf_counter() - t
+        return {"value": self.step_bytes / dt / 1e12, "unit": self.unit,
+                "cores": O.max_threads(), "kind": "port", "sample": "1 full step",
+                "seconds": round(dt, 4)}
+
+    def shape_tuple(self):
+        s = self.shape
+        return (s.batch, s.query_heads, s.kv_heads, s.dim, s.max_pages, s.physical_pages)
+
+    def reference_step(self, pool):
+        O = oracle_module()
+        t = time.perf_counter()
+        O.ref_cpu_tree_reference(self.shape_tuple(), self.N, self.dq, self.k, self.v,
+                                 self.pages, self.lengths, self.dk, self.dv, self.parent)
+        return time.perf_counter() - t, self.step_bytes, 1
+
+
+class Decode:
+    """paged split-KV decode of `batch` one-token requests
+    over `context` tokens each (pages in a seeded random permutation)."""
+
+    name = "decode"
+    flush = False
+    higher_is_better = True
+    unit = "tokens/s"
+
+    def __init__(self, torch, C, device, rank, world, batch=0, context=0, splits=0, **_):
+        self.torch, self.C, self.device = torch, C, device
+        batch, context = batch or 4, context or 131072
+        self.batch, self.context = batch, context
+        g = torch.Generator(device=device)
+        g.manual_seed(3 + rank)
+        npg = context // 16
+        P = batch * npg + 8
+        self.k = torch.randn(P, 16, 8, 128, device=device, dtype=torch.float16, generator=g)
+        self.v = torch.randn(P, 16, 8, 128, device=device, dtype=torch.float16, generator=g)
+        perm = torch.randperm(P, device=device, generator=g).to(torch.int32)
+        self.pages = perm[:batch * npg].view(batch, npg).contiguous()
+        self.lengths = torch.full((batch,), context, device=device, dtype=torch.int32)
+        self.shape = C.make_shape(batch, 32, 8, 128, npg, P)
+        self.splits = splits or C.auto_splits(self.shape, context, 148)
+        rows = batch * 32
+        self.pa = torch.empty(self.splits * rows * 128, device=device)
+        self.pml = torch.empty(self.splits * rows * 2, device=device)
+        self.q_host = torch.randn(batch, 32, 128, dtype=torch.float16).pin_memory()
+        self.q = self.q_host.to(device)
+        self.out = torch.empty(batch, 32, 128, device=device)
+        self.out_host = torch.empty(self.out.shape).pin_memory()
+        self.launches = 1 + (self.splits > 8)
+        self.kernel_bytes = batch * context * 4096 + rows * 128 * 2 + rows * 128 * 4
+        self.step_bytes = self.kernel_bytes
+        self.kernel = "attn_kernel (paged decode) + merge"
+        self.bound = "hbm"
+
+    def device_step(self, kev=None):
+        if kev:
+            kev[0].record()
+        self.C.decode(self.shape, self.q, self.k, self.v, self.pages, self.lengths, self.out,
+                      self.pa, self.pml, self.splits)
+        if kev:
+            kev[1].record()
+
+    def e2e_step(self):
+        self.q.copy_(self.q_host, non_blocking=True)
+        self.device_step()
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    def io_bytes(self):
+        return self.q_host.numel() * 2, self.out_host.numel() * 4
+
+    def value(self, steps_all_ranks, seconds):
+        return self.batch * steps_all_ranks / seconds
+
+    def config(self):
+        return {"workload": f"BASELINE config 3: paged GQA split-KV decode, batch {self.batch} x "
+                            f"context {self.context}, Hq=32 Hkv=8 D=128",
+                "splits": self.splits, "kv_bytes": self.batch * self.context * 4096}
+
+    def _sample(self, tokens):
+        """Host copy of request 0's first `tokens` tokens as a compact fixture."""
+        torch = self.torch
+        npg = tokens // 16
+        ids = self.pages[0, :npg].long()
+        k = half_bits(torch, self.k[ids])
+        v = half_bits(torch, self.v[ids])
+        q = half_bits(torch, self.q[:1])
+        pages = np.arange(npg, dtype=np.int32).reshape(1, -1)
+        return (1, 32, 8, 128, npg, npg), q, k, v, pages, np.array([tokens], np.int32)
+
+    def cpu_baseline(self, tokens=16384):
+        O = oracle_module()
+        s, q, k, v, pages, lengths = self._sample(tokens)
+        t = time.perf_counter()
+        O.decode(s, q, k, v, pages, lengths, threads=O.max_threads())
+        dt = time.perf_counter() - t
+        per_step = dt * (self.context / tokens) * self.batch
+        return {"value": self.batch / per_step, "unit": self.unit, "cores": O.max_threads(),
+                "kind": "port", "sample": f"request 0, first {tokens} tokens, scaled linearly "
+                                          f"to {self.batch} x {self.context}",
+                "seconds": round(dt, 4)}
+
+    def reference_step(self, pool, tokens=8192):
+        O = oracle_module()
+        s, q, k, v, pages, lengths = self._sample(tokens)
+        t = time.perf_counter()
+        O.ref_cpu_reference(s, q, k, v, pages, lengths)
+        dt = (time.perf_counter() - t) * (self.context / tokens) * self.batch
+        return dt, self.step_bytes, self.batch
+
+
+class Packed(Decode):
+    """vLLM-layout packed decode, B=256, lengths U[512, 8192]."""
+
+    name = "packed"
+
+    def __init__(self, torch, C, device, rank, world, batch=0, **_):
+        self.torch, self.C, self.device = torch, C, device
+        batch = batch or 256
+        rng = np.random.default_rng(256 + rank)
+        lens = rng.integers(512, 8193, size=batch).astype(np.int32)
+        npg = (lens + 15) // 16
+        nb, mp = int(npg.sum()), int(npg.max())
+        perm = rng.permutation(nb).astype(np.int32)
+        pages = np.full((batch, mp), -1, np.int32)
+        cur = 0
+        for b in range(batch):
+            pages[b, :npg[b]] = perm[cur:cur + npg[b]]
+            cur += npg[b]
+        g = torch.Generator(device=device)
+        g.manual_seed(4 + rank)
+        self.cache = torch.randn(nb, 2, 16, 8, 128, device=device, dtype=torch.float16,
+                                 generator=g)
+        self.pages = torch.from_numpy(pages).to(device)
+        self.lengths = torch.from_numpy(lens).to(device)
+        self.lens = lens
+        self.batch = batch
+        self.shape = C.make_shape(batch, 32, 8, 128, mp, nb)
+        self.q_host = torch.randn(batch, 32, 128, dtype=torch.float16).pin_memory()
+        self.q = self.q_host.to(device)
+        self.out = torch.empty(batch, 32, 128, device=device, dtype=torch.float16)
+        self.out_host = torch.empty(self.out.shape, dtype=torch.float16).pin_memory()
+        self.launches = 1
+        rows = batch * 32
+        self.kernel_bytes = int(lens.sum()) * 4096 + rows * 128 * 2 * 2 + batch * mp * 4
+        self.step_bytes = self.kernel_bytes
+        self.kernel = "attn_kernel (packed decode)"
+        self.bound = "hbm"
+
+    def device_step(self, kev=None):
+        if kev:
+            kev[0].record()
+        self.C.packed_decode_kv(self.shape, self.q, self.cache, self.pages, self.lengths,
+                                self.out, 2 * 16 * 8 * 128, 128, 8 * 128, 16 * 8 * 128, SCALE, 0)
+        if kev:
+            kev[1].record()
+
+    def io_bytes(self):
+        return self.q_host.numel() * 2, self.out_host.numel() * 2
+
+    def config(self):
+        return {"workload": "BASELINE config 4: vLLM-layout [num_blocks,2,16,8,128] packed "
+                            "decode, batch 256, lengths U[512,8192] (seeded)",
+                "tokens": int(self.lens.sum()), "kv_bytes": int(self.lens.sum()) * 4096}
+
+    def cpu_baseline(self, requests=8):
+        O = oracle_module()
+        torch = self.torch
+        # the first `requests` requests, their pages copied to a compact host cache
+        pages = self.pages[:requests].cpu().numpy()
+        used = sorted({int(p) for p in pages.ravel() if p >= 0})
+        remap = {p: i for i, p in enumerate(used)}
+        cache = half_bits(torch, self.cache[torch.tensor(used, device=self.device)])
+        pages = np.vectorize(lambda p: remap.get(int(p), -1))(pages).astype(np.int32)
+        q = half_bits(torch, self.q[:requests])
+        s = (requests, 32, 8, 128, pages.shape[1], len(used))
+        t = time.perf_counter()
+        O.packed_decode(s, q, cache, pages, self.lens[:requests], 2 * 16 * 8 * 128, 128,
+                        8 * 128, 16 * 8 * 128, SCALE, threads=O.max_threads())
+        dt = time.perf_counter() - t
+        return {"value": requests / dt, "unit": self.unit, "cores": O.max_threads(),
+                "kind": "port", "sample": f"the first {requests} requests of the batch",
+                "seconds": round(dt, 4)}
+
+    def reference_step(self, pool):
+        return None
+
+
+class TreeScale:
+    """BASELINE config 5a: 1024 requests (split across ranks), each a 63-node
+    full binary tree over a 4096-token prefix shared by groups of 16 requests;
+    FP16 output. Tensor-bound: value = whole-job TFLOP/s."""
+
+    name = "tree-scale"
+    flush = False
+    higher_is_better = True
+    unit = "TFLOP/s"
+
+    def __init__(self, torch, C, device, rank, world, total=1024, group=16, prefix=4096,
+                 nodes=63, **_):
+        from bc_dist import shard_requests
+
+        self.torch, self.C, self.device = torch, C, device
+        reqs = shard_requests(total // group, world, rank)  # whole prefix groups
+        ngroups = len(reqs)
+        B = ngroups * group
+        self.B, self.N, self.prefix, self.group = B, nodes, prefix, group
+        npg = prefix // 16
+        P = ngroups * npg + 8
+        g = torch.Generator(device=device)
+        g.manual_seed(55 + rank)
+        self.k = torch.randn(P, 16, 8, 128, device=device, dtype=torch.float16, generator=g)
+        self.v = torch.randn(P, 16, 8, 128, device=device, dtype=torch.float16, generator=g)
+        perm = torch.randperm(P, device=device, generator=g).to(torch.int32)
+        gp = perm[:ngroups * npg].view(ngroups, npg)
+        self.pages = gp.repeat_interleave(group, dim=0).contiguous()
+        self.lengths = torch.full((B,), prefix, device=device, dtype=torch.int32)
+        self.dq = torch.randn(B, nodes, 32, 128, device=device, dtype=torch.float16, generator=g)
+        self.dk = torch.randn(B, nodes, 8, 128, device=device, dtype=torch.float16, generator=g)
+        self.dv = torch.randn(B, nodes, 8, 128, device=device, dtype=torch.float16, generator=g)
+        par = [-1] + [(n - 1) // 2 for n in range(1, nodes)]
+        self.parent = torch.tensor([par] * B, device=device, dtype=torch.int32)
+        self.shape = C.make_shape(B, 32, 8, 128, npg, P)
+        self.out = torch.empty(B, nodes, 32, 128, device=device, dtype=torch.float16)
+        depth_sum = sum(int(math.log2(n + 1)) + 1 for n in range(nodes))
+        self.flops = 32 * 4 * 128 * B * (nodes * prefix + depth_sum)
+        self.unique_bytes = (ngroups * prefix * 4096 + B * nodes * 8 * 128 * 4
+                             + B * nodes * 32 * 128 * 4 + B * npg * 4)
+        self.launches = 1
+        self.kernel = "tree_mma_kernel (tree_verify, FP16 out)"
+        self.bound = "tensor"
+        # end-to-end leg: this step's draft tensors and tables from pinned host
+        # memory, the FP16 verdict tensor back
+        self.host = {n: getattr(self, n).cpu().pin_memory()
+                     for n in ("dq", "dk", "dv", "parent", "pages", "lengths")}
+        self.out_host = torch.empty(self.out.shape, dtype=torch.float16).pin_memory()
+
+    def device_step(self, kev=None):
+        if kev:
+            kev[0].record()
+        self.C.tree_verify(self.shape, self.dq, self.k, self.v, self.pages, self.lengths,
+                           self.dk, self.dv, self.parent, self.out, self.N)
+        if kev:
+            kev[1].record()
+
+    def e2e_step(self):
+        for n, t in self.host.items():
+            getattr(self, n).copy_(t, non_blocking=True)
+        self.device_step()
+        self.out_host.copy_(self.out, non_blocking=True)
+
+    def io_bytes(self):
+        return (sum(t.numel() * t.element_size() for t in self.host.values()),
+                self.out_host.numel() * 2)
+
+    def value(self, steps_all_ranks, seconds):
+        return self.flops * steps_all_ranks / seconds / 1e12
+
+    def config(self):
+        return {"workload": "BASELINE config 5a: tree_verify, 1024 requests x 63-node full "
+                            "binary trees, 4096-token prefix shared per 16 requests, FP16 out",
+                "requests_per_gpu": self.B, "flops_per_step": self.flops,
+                "unique_bytes_per_step": self.unique_bytes, "parallelism": "request-sharded"}
+
+    def cpu_baseline(self):
+        O = oracle_module()
+        torch = self.torch
+        npg = self.prefix // 16
+        ids = self.pages[0].long()
+        k, v = half_bits(torch, self.k[ids]), half_bits(torch, self.v[ids])
+        s = (1, 32, 8, 128, npg, npg)
+        pages = np.arange(npg, dtype=np.int32).reshape(1, -1)
+        t = time.perf_counter()
+        O.tree(s, self.N, half_bits(torch, self.dq[:1]), k, v, pages,
+               np.array([self.prefix], np.int32), half_bits(torch, self.dk[:1]),
+               half_bits(torch, self.dv[:1]), self.parent[:1].cpu().numpy(),
+               threads=O.max_threads())
+        dt = time.perf_counter() - t
+        return {"value": (self.flops / self.B) / dt / 1e12, "unit": self.unit,
+                "cores": O.max_threads(), "kind": "port",
+                "sample": "1 request (63 nodes x 4096-token prefix)", "seconds": round(dt, 4)}
+
+    def reference_step(self, pool):
+        return None
+
+
+class LongCtx:
+    """BASELINE config 5b: one request of 1,048,576 tokens; rank r holds a
+    contiguous 1/world shard of its pages and reduces it to FP32 partials
+    (m, l, acc) — `splits` of them per q-head, unmerged, when splits > 8 —
+    which are all-gathered over NCCL and merged on the device in one launch.
+    value = tokens/s (one decoded token per job step); strong scaling."""
+
+    name = "longctx"
+    flush = False
+    higher_is_better = True
+    unit = "tokens/s"
+
+    def __init__(self, torch, C, device, rank, world, total=1 << 20, splits=0, **_):
+        from bc_dist import shard_pages
+
+        self.torch, self.C, self.device, self.world = torch, C, device, world
+        npg_total = total // 16
+        mine = shard_pages(npg_total, world, rank)
+        npg = len(mine)
+        g = torch.Generator(device=device)
+        g.manual_seed(77 + rank)
+        P = npg + 8
+        self.k = torch.randn(P, 16, 8, 128, device=device, dtype=torch.float16, generator=g)
+        self.v = torch.randn(P, 16, 8, 128, device=device, dtype=torch.float16, generator=g)
+        perm = torch.randperm(P, device=device, generator=g).to(torch.int32)
+        self.pages = perm[:npg].view(1, npg).contiguous()
+        self.lengths = torch.tensor([npg * 16], device=device, dtype=torch.int32)
+        self.shape = C.make_shape(1, 32, 8, 128, npg, P)
+        # enough CTAs (8 KV heads x splits) for two per SM unless told otherwise
+        self.splits = splits or min(C.MAX_SPLITS, max(9, -(-2 * 148 // 8)))
+        self.S = self.splits if self.splits > 8 else 1
+        gq = torch.Generator()
+        gq.manual_seed(5)
+        self.q_host = torch.randn(1, 32, 128, dtype=torch.float16, generator=gq).pin_memory()
+        self.q = self.q_host.to(device)
+        self.out_host = torch.empty(1, 32, 128).pin_memory()
+        self.pml = torch.empty(self.S, 32, 2, device=device)
+        self.pa = torch.empty(self.S, 32, 128, device=device)
+        self.g_ml = torch.empty(world, self.S, 32, 2, device=device)
+        self.g_a = torch.empty(world, self.S, 32, 128, device=device)
+        self.out = torch.empty(32, 128, device=device)
+        self.total = total
+        self.kernel_bytes = npg * 16 * 4096 + 32 * 128 * 2 + self.S * 32 * 130 * 4
+        self.step_bytes = self.kernel_bytes
+        self.launches = 2  # rank-local partial decode + merge of every partial
+        self.kernel = "attn_kernel (paged decode partial)"
+        self.bound = "hbm"
+
+    def device_step(self, kev=None):
+        C = self.C
+        if kev:
+            kev[0].record()
+        C.paged_decode_partial(self.shape, self.q, self.k, self.v, self.pages, self.lengths,
+                               self.pml, self.pa, self.splits)
+        if kev:
+            kev[1].record()
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(self.g_ml, self.pml)
+            dist.all_gather_into_tensor(self.g_a, self.pa)
+            g_ml, g_a = self.g_ml, self.g_a
+        else:
+            g_ml, g_a = self.pml.unsqueeze(0), self.pa.unsqueeze(0)
+        n = self.world * self.S
+        C.merge_partials(g_ml.view(n, 32, 2), g_a.view(n, 32, 128), self.out)
+
+    def e2e_step(self):
+        self.q.copy_(self.q_host, non_blocking=True)
+        self.device_step()
+        self.out_host.view(32, 128).copy_(self.out, non_blocking=True)
+
+    def io_bytes(self):
+        return self.q_host.numel() * 2, self.out_host.numel() * 4
+
+    def value(self, steps_all_ranks, seconds):
+        return (steps_all_ranks / self.world) / seconds  # one token per job step
+
+    def config(self):
+        return {"workload": "BASELINE config 5b: one request, 1,048,576-token context split "
+                            "across ranks, FP32 partials all-gathered (NCCL) and merged",
+                "tokens_per_gpu": int(self.lengths[0]), "splits_per_gpu": self.splits,
+                "parallelism": f"context-split x{self.world}",
+                "collective_bytes_per_rank": self.S * 32 * (128 + 2) * 4}
+
+    def cpu_baseline(self, tokens=65536):
+        O = oracle_module()
+        torch = self.torch
+        npg = tokens // 16
+        ids = self.pages[0, :npg].long()
+        k, v = half_bits(torch, self.k[ids]), half_bits(torch, self.v[ids])
+        s = (1, 32, 8, 128, npg, npg)
+        t = time.perf_counter()
+        O.decode(s, half_bits(torch, self.q), k, v, np.arange(npg, dtype=np.int32).reshape(1, -1),
+                 np.array([tokens], np.int32), threads=O.max_threads())
+        dt = (time.perf_counter() - t) * self.total / tokens
+        return {"value": 1 / dt, "unit": self.unit, "cores": O.max_threads(), "kind": "port",
+                "sample": f"a {tokens}-token slice, scaled linearly to {self.total} tokens",
+                "seconds": round(dt, 4)}
+
+    def reference_step(self, pool):
+        return None
+
+
+WORKLOADS = {w.name: w for w in (TreeCow, TreeOracle, Decode, Packed, TreeScale, LongCtx)}
 
 
 # --------------------------------------------------------------- our arm
@@ -154,62 +758,12 @@ def run_ours(args):
     device = torch.device("cuda", torch.cuda.current_device())
 
     import bc_capi as C
-    from bc_workloads import TreeCowWorkload
 
-    hbm_peak, _, peak_kind = load_peaks()
-    wl = TreeCowWorkload(seed=2040 + rank)
-    plan, _ = wl.plan()
-    shape = C.make_shape(*wl.shape())
-    k0, v0 = wl.initial_cache()
-    cache_k, cache_v = to_dev(torch, k0, device), to_dev(torch, v0, device)
-    host = {  # per-step inputs, pinned for the end-to-end leg
-        "draft_q": pinned(torch, wl.draft_q), "draft_k": pinned(torch, wl.draft_k),
-        "draft_v": pinned(torch, wl.draft_v), "parent": pinned(torch, wl.parent),
-        "pages": pinned(torch, wl.pages), "lengths": pinned(torch, wl.lengths),
-        "clone_src": pinned(torch, np.array(plan.clone_src, np.int32)),
-        "clone_dst": pinned(torch, np.array(plan.clone_dst, np.int32)),
-        "e_req": pinned(torch, np.array(plan.entry_request, np.int32)),
-        "e_node": pinned(torch, np.array(plan.entry_node, np.int32)),
-        "e_page": pinned(torch, np.array(plan.entry_page, np.int32)),
-        "e_slot": pinned(torch, np.array(plan.entry_slot, np.int32)),
-    }
-    dev = {n: t.to(device) for n, t in host.items()}
-    out = torch.empty(wl.batch, wl.nodes, wl.hq, wl.dim, device=device, dtype=torch.float32)
-    out_host = torch.empty(out.shape, dtype=torch.float32).pin_memory()
-    flush = torch.empty(FLUSH_BYTES // 4, device=device, dtype=torch.float32)
+    hbm_peak, tensor_peak, peak_kind = load_peaks()
+    wl = WORKLOADS[args.workload](torch, C, device, rank, world, batch=args.batch,
+                                  context=args.context, splits=args.splits)
+    flush = torch.empty(FLUSH_BYTES // 4, device=device) if wl.flush else None
     stream = torch.cuda.current_stream()
-
-    launches_per_step = 1 + (1 if plan.clone_src else 0) + (1 if plan.entry_node else 0)
-
-    def device_step(t_ev=None):
-        if t_ev:
-            t_ev[0].record(stream)
-        C.tree_verify(shape, dev["draft_q"], cache_k, cache_v, dev["pages"], dev["lengths"],
-                      dev["draft_k"], dev["draft_v"], dev["parent"], out, wl.nodes)
-        if t_ev:
-            t_ev[1].record(stream)
-        C.commit_batch(shape, wl.nodes, dev["draft_k"], dev["draft_v"], cache_k, cache_v,
-                       dev["clone_src"], dev["clone_dst"], dev["e_req"], dev["e_node"],
-                       dev["e_page"], dev["e_slot"])
-
-    def e2e_step():
-        for n, t in host.items():
-            dev[n].copy_(t, non_blocking=True)
-        device_step()
-        out_host.copy_(out, non_blocking=True)
-
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = out_host.numel() * out_host.element_size()
-
-    # Correctness gate before timing: the first step against the oracle on
-    # rank 0 is done by the test-suite; here only the device error word.
-    for _ in range(args.warmup):
-        flush.fill_(1.0)
-        device_step()
-        e2e_step()
-    torch.cuda.synchronize()
-    if C.last_device_error() != 0:
-        raise SystemExit("device error word set during warm-up")
 
     def barrier():
         if world > 1:
@@ -218,106 +772,89 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    for _ in range(args.warmup):
+        if flush is not None:
+            flush.fill_(1.0)
+        wl.device_step()
+        wl.e2e_step()
+    torch.cuda.synchronize()
+    if C.last_device_error() != 0:
+        raise SystemExit("device error word set during warm-up")
+
     sampler = ClockSampler(device.index)
     time.sleep(0.3)
-    # ---- device-resident timed region
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    tev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
+    steps = Events(torch, args.steps)
+    kern = Events(torch, args.steps)
     barrier()
     t0 = time.time()
     for i in range(args.steps):
-        flush.fill_(1.0)
-        evs[i][0].record(stream)
-        device_step(tev[i])
-        evs[i][1].record(stream)
+        if flush is not None:
+            flush.fill_(1.0)
+        steps.ev[i][0].record(stream)
+        wl.device_step(kern.ev[i])
+        steps.ev[i][1].record(stream)
     barrier()
     t1 = time.time()
-    step_ms = [a.elapsed_time(b) for a, b in evs]
-    tree_ms = [a.elapsed_time(b) for a, b in tev]
-    # ---- end-to-end timed region (pinned host inputs -> device -> host output)
-    eevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            for _ in range(args.steps)]
+    e2e = Events(torch, args.steps)
     barrier()
     for i in range(args.steps):
-        flush.fill_(1.0)
-        eevs[i][0].record(stream)
-        e2e_step()
-        eevs[i][1].record(stream)
+        if flush is not None:
+            flush.fill_(1.0)
+        e2e.ev[i][0].record(stream)
+        wl.e2e_step()
+        e2e.ev[i][1].record(stream)
     barrier()
     sampler.stop()
-    e2e_ms = [a.elapsed_time(b) for a, b in eevs]
     err = C.last_device_error()
-
-    total_ms = sum(step_ms)
-    total_e2e_ms = sum(e2e_ms)
+    step_ms, kern_ms, e2e_ms = steps.ms(), kern.ms(), e2e.ms()
+    total_ms, total_e2e = sum(step_ms), sum(e2e_ms)
     if world > 1:
         import torch.distributed as dist
 
-        t = torch.tensor([total_ms, total_e2e_ms], device=device, dtype=torch.float64)
+        t = torch.tensor([total_ms, total_e2e, float(err)], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, total_e2e_ms = float(t[0]), float(t[1])
-        e = torch.tensor([err], device=device, dtype=torch.int64)
-        dist.all_reduce(e, op=dist.ReduceOp.MAX)
-        err = int(e[0])
+        total_ms, total_e2e, err = float(t[0]), float(t[1]), int(t[2])
 
-    step_bytes = wl.verify_bytes() + wl.commit_bytes(plan)
-    all_bytes = step_bytes * args.steps * world
-    value_tbs = all_bytes / (total_ms * 1e-3) / 1e12
-    e2e_tbs = all_bytes / (total_e2e_ms * 1e-3) / 1e12
-    tree_us = statistics.mean(tree_ms) * 1e3
-    achieved_gbs = wl.verify_bytes() / (tree_us * 1e-6) / 1e9
-    clocks = sampler.window(t0, t1)
-
+    value = wl.value(args.steps * world, total_ms * 1e-3)
+    e2e_value = wl.value(args.steps * world, total_e2e * 1e-3)
+    kern_us = statistics.mean(kern_ms) * 1e3
+    if wl.bound == "tensor":
+        achieved = wl.flops / (kern_us * 1e-6) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tensor_peak,
+                "unit": "TFLOP/s", "frac": round(achieved / tensor_peak, 4),
+                "peak_source": f"{peak_kind} bf16_tflops (FP16 = BF16 rate)"}
+    else:
+        achieved = wl.kernel_bytes / (kern_us * 1e-6) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak,
+                "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                "peak_source": f"{peak_kind} hbm_gbs"}
+    roof["kernel"] = wl.kernel
+    roof["kernel_us"] = round(kern_us, 3)
+    roof["traffic"] = args.traffic
+    h2d, d2h = wl.io_bytes()
+    cfg = wl.config()
+    cfg["l2"] = ("flushed between timed steps (256 MiB device write, outside the step events)"
+                 if wl.flush else "inputs larger than L2 (no flush)")
+    cfg.setdefault("parallelism", f"request-sharded x{world}")
     if rank == 0:
         line = {
-            "metric": METRIC,
-            "value": round(value_tbs, 6),
-            "unit": "TB/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
+            "metric": METRIC, "value": round(value, 6), "unit": wl.unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(total_ms / args.steps, 6),
-            "higher_is_better": True,
-            "scaling": "weak",
-            "vs_baseline": None,
-            "dtype": "f16 in / f32 accumulate",
-            "data": "synthetic (seeded N(0,1) FP16, per-rank seed)",
-            "config": {
-                "workload": "BASELINE config 2: batched shared-prefix tree_verify + COW "
-                            "commit_path_ (8 requests, shared 2040-token prefix, 7-node "
-                            "random trees, Hq=32 Hkv=8 D=128, page 16)",
-                "requests_per_gpu": wl.batch, "prefix_tokens": wl.prefix,
-                "tree_nodes": wl.nodes, "parallelism": f"request-sharded x{world}",
-                "l2": "flushed between timed steps (256 MiB device write, outside the "
-                      "step events)",
-                "step_bytes": step_bytes,
-                "tree_verify_us": round(tree_us, 3),
-                "verify_bytes_per_launch": wl.verify_bytes(),
-                "verify_flops_per_launch": wl.verify_flops(),
-                "commit_clones": len(plan.clone_src),
-                "commit_rows": len(plan.entry_node),
-            },
-            "e2e": {"value": round(e2e_tbs, 6), "unit": "TB/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": round(total_e2e_ms / args.steps, 6)},
-            "gpu_launches": launches_per_step * args.steps,
-            "roofline": {
-                "kernel": "attn_kernel (tree_verify)",
-                "bound": "hbm",
-                "achieved": round(achieved_gbs, 2),
-                "peak": hbm_peak,
-                "unit": "GB/s",
-                "frac": round(achieved_gbs / hbm_peak, 4),
-                "peak_source": f"{peak_kind} hbm_gbs",
-                "traffic": args.traffic,
-            },
-            "clocks": clocks,
-            "device_error_word": err,
+            "higher_is_better": wl.higher_is_better,
+            "scaling": "strong" if wl.name in ("tree-scale", "longctx") else "weak",
+            "vs_baseline": None, "dtype": "f16 in / f32 accumulate",
+            "data": "synthetic (seeded N(0,1) FP16, per-rank seed)", "config": cfg,
+            "e2e": {"value": round(e2e_value, 6), "unit": wl.unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(total_e2e / args.steps, 6)},
+            "gpu_launches": wl.launches * args.steps,
+            "roofline": roof, "clocks": sampler.window(t0, t1), "device_error_word": err,
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_tree_cow(wl, plan, step_bytes)
+            cb = wl.cpu_baseline()
+            cb["value"] = float(f"{cb['value']:.6g}")
+            line["cpu_baseline"] = cb
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -326,102 +863,72 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-# --------------------------------------------------------------- CPU legs
-def cpu_baseline_tree_cow(wl, plan, step_bytes):
-    """The oracle port (oracle/bc_oracle.cpp, OpenMP over rows) timed on one
-    full step of the same workload: tree verify + sequential COW commits."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle as O
-    from cow_oracle import CowOracle
-
-    threads = O.max_threads()
-    k0, v0 = wl.initial_cache()
-    t = time.perf_counter()
-    O.tree(wl.shape(), wl.nodes, wl.draft_q, k0, v0, wl.pages, wl.lengths, wl.draft_k,
-           wl.draft_v, wl.parent, threads=threads)
-    cow = CowOracle(wl.pool_pages, wl.hkv, wl.dim)
-    r0 = cow.new(wl.prefix_k, wl.prefix_v)
-    reqs = [r0] + [cow.fork(r0) for _ in range(wl.batch - 1)]
-    for b in range(wl.batch):
-        cow.commit(reqs[b], wl.paths[b], wl.draft_k[b], wl.draft_v[b])
-    dt = time.perf_counter() - t
-    return {"value": round(step_bytes / dt / 1e12, 9), "unit": "TB/s", "cores": threads,
-            "kind": "port", "sample": "1 full step (8-request tree verify + 8 COW commits)",
-            "seconds": round(dt, 4)}
-
-
+# --------------------------------------------------------------- reference arm
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle as O
+    O = oracle_module()
+    if not O.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libbcref.so (the "
+                                                            "reference built from its sources) is missing"}))
+        return
+    if args.workload not in ("tree-cow", "tree-oracle", "decode"):
+        print(json.dumps({"impl": "reference", "unavailable": f"no reference CPU path measured "
+                                                            f"for workload {args.workload}"}))
+        return
     from concurrent.futures import ThreadPoolExecutor
 
-    from bc_workloads import TreeCowWorkload
-    from cow_oracle import CowOracle
+    import torch
 
-    if not O.ref_available():
-        print(json.dumps({"impl": "reference",
-                          "unavailable": "oracle/_ref/libbcref.so (the reference built from its "
-                                         "sources) is missing"}))
-        return
-    wl = TreeCowWorkload(seed=2040)
-    plan, _ = wl.plan()
-    k0, v0 = wl.initial_cache()
-    step_bytes = wl.verify_bytes() + wl.commit_bytes(plan)
-    cores = min(wl.batch, os.cpu_count() or 1)
+    device = torch.device("cuda", 0) if torch.cuda.is_available() else None
+    if args.workload == "tree-cow":
+        wl = TreeCow.__new__(TreeCow)
+        from bc_workloads import TreeCowWorkload
 
-    def one_request(b):
-        s = (1, wl.hq, wl.hkv, wl.dim, wl.max_pages, wl.pool_pages)
-        return O.ref_cpu_tree_reference(s, wl.nodes, wl.draft_q[b:b + 1], k0, v0,
-                                        wl.pages[b:b + 1], wl.lengths[b:b + 1],
-                                        wl.draft_k[b:b + 1], wl.draft_v[b:b + 1],
-                                        wl.parent[b:b + 1])
+        wl.wl = TreeCowWorkload(seed=2040)
+        wl.plan, _ = wl.wl.plan()
+        wl.step_bytes = wl.wl.verify_bytes() + wl.wl.commit_bytes(wl.plan)
+        unit = TreeCow.unit
+    else:
+        if device is None:
+            print(json.dumps({"impl": "reference", "unavailable": "this workload's inputs are "
+                                                                "generated on a GPU"}))
+            return
+        import bc_capi as C
 
-    def step(pool):
-        list(pool.map(one_request, range(wl.batch)))
-        cow = CowOracle(wl.pool_pages, wl.hkv, wl.dim)
-        r0 = cow.new(wl.prefix_k, wl.prefix_v)
-        reqs = [r0] + [cow.fork(r0) for _ in range(wl.batch - 1)]
-        for b in range(wl.batch):
-            cow.commit(reqs[b], wl.paths[b], wl.draft_k[b], wl.draft_v[b])
-
+        wl = WORKLOADS[args.workload](torch, C, device, 0, 1)
+        unit = wl.unit
+    cores = min(8, os.cpu_count() or 1)
+    times, bytes_, units = [], 0, 0
     with ThreadPoolExecutor(max_workers=cores) as pool:
         for _ in range(args.warmup):
-            step(pool)
-        times = []
+            wl.reference_step(pool)
         for _ in range(args.steps):  # bounded: stop once the CPU budget is spent
-            t = time.perf_counter()
-            step(pool)
-            times.append(time.perf_counter() - t)
+            dt, b, u = wl.reference_step(pool)
+            times.append(dt)
+            bytes_ += b
+            units += u
             if sum(times) > args.reference_budget_s:
                 break
     total = sum(times)
-    value = step_bytes * len(times) / total / 1e12
+    value = bytes_ / total / 1e12 if unit == "TB/s" else units / total
     print(json.dumps({
-        "impl": "reference",
-        "metric": METRIC,
-        "value": round(value, 9),
-        "unit": "TB/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(total / len(times) * 1e3, 3),
-        "steps_timed": len(times),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
+        "impl": "reference", "metric": METRIC, "value": float(f"{value:.6g}"), "unit": unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / len(times) * 1e3, 3), "steps_timed": len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 in / f64 accumulate (reference CPU oracle)",
-        "data": "synthetic (seeded N(0,1) FP16)",
-        "config": {"workload": "BASELINE config 2 (same inputs as the CUDA arm, rank 0 seed)",
-                   "step_bytes": step_bytes},
-        "cpu_baseline": {"value": round(value, 9), "unit": "TB/s", "cores": cores,
+        "data": "synthetic (seeded N(0,1) FP16, same inputs as the CUDA arm's rank 0)",
+        "config": wl.config(),
+        "cpu_baseline": {"value": float(f"{value:.6g}"), "unit": unit, "cores": cores,
                          "kind": "reference",
-                         "sample": "each step = the full 8-request step: the reference's "
-                                   "cpu_tree_reference (one request per host thread) + "
-                                   "the sequential COW commits"},
-        "e2e": {"value": round(value, 9), "unit": "TB/s", "h2d_bytes_per_step": 0,
+                         "sample": "tree-cow: each step = the full 8-request step (the "
+                                   "reference's cpu_tree_reference, one request per host "
+                                   "thread, + the sequential COW commits)"
+                                   if args.workload == "tree-cow" else
+                                   "a bounded slice of the step, scaled linearly"},
+        "e2e": {"value": float(f"{value:.6g}"), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -429,15 +936,21 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="tree-cow")
     ap.add_argument("--traffic", type=float, default=None,
-                    help="ncu-measured DRAM bytes per tree_verify launch, if known")
+                    help="ncu-measured DRAM bytes per launch of the dominant kernel, if known")
+    ap.add_argument("--batch", type=int, default=0, help="decode/packed batch (0: config's)")
+    ap.add_argument("--context", type=int, default=0, help="decode context tokens (0: 131072)")
+    ap.add_argument("--splits", type=int, default=0, help="decode/longctx KV splits (0: auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reference-budget-s", type=float, default=60.0,
                     help="CPU seconds after which the reference arm stops timing steps")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = {"tree-cow": 2000, "tree-oracle": 2000}.get(args.workload, 50)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":

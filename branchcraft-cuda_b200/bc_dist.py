@@ -30,22 +30,28 @@ def shard_pages(num_pages: int, world: int, rank: int) -> range:
 def split_kv_decode(local_partial, merge, all_gather, rows: int, dim: int, world: int):
     """Run one distributed decode step.
 
-    local_partial() -> (partial_ml [rows, 2], partial_a [rows, dim]) of this rank
+    local_partial() -> (partial_ml [S, rows, 2], partial_a [S, rows, dim]) of
+                       this rank, S >= 1 partials per row (a 2-D pair means S = 1)
     all_gather(t)   -> tensor [world, *t.shape] gathered from every rank
-    merge(pml [world, rows, 2], pa [world, rows, dim]) -> out [rows, dim]
+    merge(pml [world*S, rows, 2], pa [world*S, rows, dim]) -> out [rows, dim]
     """
     pml, pa = local_partial()
-    assert tuple(pml.shape) == (rows, 2) and tuple(pa.shape) == (rows, dim)
+    if pml.dim() == 2:
+        pml, pa = pml.unsqueeze(0), pa.unsqueeze(0)
+    S = pml.shape[0]
+    assert tuple(pml.shape) == (S, rows, 2) and tuple(pa.shape) == (S, rows, dim)
     g_ml = all_gather(pml)
     g_a = all_gather(pa)
-    assert tuple(g_ml.shape) == (world, rows, 2)
-    return merge(g_ml, g_a)
+    assert tuple(g_ml.shape) == (world, S, rows, 2)
+    return merge(g_ml.reshape(world * S, rows, 2), g_a.reshape(world * S, rows, dim))
 
 
 def cuda_split_kv_decode(shape, q, k, v, pages, lengths, group, splits: int = 0):
     """Production path: bc_paged_decode_partial on this rank's shard, NCCL
     all_gather_into_tensor, bc_merge_partials. `shape`, `pages`, `lengths`
-    describe this rank's shard; returns FP32 [B, Hq, D] on every rank."""
+    describe this rank's shard; returns FP32 [B, Hq, D] on every rank.
+    `splits` > 8 keeps that many unmerged partials per row on every rank (all
+    of them are gathered and merged at once); otherwise each rank sends one."""
     import torch
     import torch.distributed as dist
 
@@ -54,10 +60,11 @@ def cuda_split_kv_decode(shape, q, k, v, pages, lengths, group, splits: int = 0)
     world = dist.get_world_size(group)
     rows = shape.batch * shape.query_heads
     dev = q.device
+    S = splits if splits > 8 else 1
 
     def local_partial():
-        pml = torch.empty(rows, 2, device=dev, dtype=torch.float32)
-        pa = torch.empty(rows, shape.dim, device=dev, dtype=torch.float32)
+        pml = torch.empty(S, rows, 2, device=dev, dtype=torch.float32)
+        pa = torch.empty(S, rows, shape.dim, device=dev, dtype=torch.float32)
         C.paged_decode_partial(shape, q, k, v, pages, lengths, pml, pa, splits)
         return pml, pa
 

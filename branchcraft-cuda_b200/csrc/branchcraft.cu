@@ -467,8 +467,8 @@ int bc_paged_decode(const bc_shape* s, const void* q, const void* k, const void*
 int bc_paged_decode_partial(const bc_shape* s, const void* q, const void* k, const void* v,
                             const int* pages, const int* lengths, float* partial_ml,
                             float* partial_a, int splits, void* stream) {
-  if (!basic_shape_ok(s) || splits > 8 || !q || !k || !v || !pages || !lengths || !partial_ml ||
-      !partial_a)
+  if (!basic_shape_ok(s) || splits > BC_MAX_SPLITS || !q || !k || !v || !pages || !lengths ||
+      !partial_ml || !partial_a)
     return cudaErrorInvalidValue;
   const int dev = current_device();
   if (dev < 0) return cudaErrorInvalidDevice;
@@ -477,10 +477,12 @@ int bc_paged_decode_partial(const bc_shape* s, const void* q, const void* k, con
     row_tiling(s->query_heads / s->kv_heads, &rt, &chunks);
     splits = auto_cluster((long long)s->batch * s->kv_heads * chunks, s->max_pages, sm_count(dev));
   }
+  // 1..8: merged inside a cluster, one partial per row. Above 8: every split
+  // stores its own partial (global mode with the merge kernel left out).
+  const int mode = splits <= 1 ? kSplitNone : splits <= 8 ? kSplitCluster : kSplitGlobal;
   return paged_decode_core(s, q, k, v, pages, lengths, nullptr, false,
-                           1.0f / std::sqrt(float(s->dim)), splits,
-                           splits > 1 ? kSplitCluster : kSplitNone, true, partial_a, partial_ml,
-                           false, nullptr, static_cast<cudaStream_t>(stream));
+                           1.0f / std::sqrt(float(s->dim)), splits, mode, true, partial_a,
+                           partial_ml, false, nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int bc_tree_verify(const bc_shape* s, const void* draft_q, const void* prefix_k,

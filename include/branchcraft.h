@@ -148,11 +148,14 @@ int bc_packed_decode_kv(const bc_shape* shape, const void* q, const void* packed
 int bc_merge_partials(int splits, int rows, int dim, const float* partial_ml,
                       const float* partial_a, float* out, void* stream);
 
-/* As bc_paged_decode but always writing this call's un-merged state as one
- * partial (m, l, acc) per (request, q-head) into partial_ml / partial_a
- * (layout of bc_merge_partials with splits = 1, rows = B*Hq): the per-GPU half
- * of a context split across GPUs. `splits` (<= 0 auto, 1..8) is the on-chip
- * split inside this GPU. Not in the reference. */
+/* As bc_paged_decode but writing this call's un-merged state as partials
+ * (m, l, acc) per (request, q-head) into partial_ml / partial_a, in the layout
+ * of bc_merge_partials with rows = B*Hq: the per-GPU half of a context split
+ * across GPUs. `splits` <= 0 (chosen by the library) or 1..8: the splits are
+ * merged on chip and the call writes ONE partial per row (splits = 1 in that
+ * layout). `splits` 9..BC_MAX_SPLITS: the call writes `splits` partials per
+ * row, unmerged, for a caller that gathers them and merges all at once (for a
+ * batch too small to fill the GPU with on-chip merges). Not in the reference. */
 int bc_paged_decode_partial(const bc_shape* shape, const void* q, const void* k,
                             const void* v, const int* pages, const int* lengths,
                             float* partial_ml, float* partial_a, int splits, void* stream);

@@ -63,14 +63,26 @@ def _worker(rank, world, port, data, result):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        q, k, v, pages, length, dim = data
+        q, k, v, pages, length, dim, per_rank = data
         shard = shard_pages(len(pages), world, rank)
         my_pages = pages[shard.start:shard.stop]
-        my_len = max(0, min(length - shard.start * 16, len(my_pages) * 16))
 
         def local():
-            pml, pa = _partial_numpy(q, k, v, my_pages, my_len, dim)
-            return torch.from_numpy(pml), torch.from_numpy(pa)
+            # `per_rank` partials per row: this rank's pages split again, as a
+            # GPU keeping its on-chip splits unmerged does.
+            mls, accs = [], []
+            for sub in shard_pages(len(my_pages), per_rank, 0), shard_pages(len(my_pages),
+                                                                            per_rank, 1):
+                if len(mls) == per_rank:
+                    break
+                start = shard.start + sub.start
+                n = max(0, min(length - start * 16, len(sub) * 16))
+                pml, pa = _partial_numpy(q, k, v, my_pages[sub.start:sub.stop], n, dim)
+                mls.append(torch.from_numpy(pml))
+                accs.append(torch.from_numpy(pa))
+            if per_rank == 1:
+                return mls[0], accs[0]
+            return torch.stack(mls), torch.stack(accs)
 
         def gather(t):
             out = [torch.empty_like(t) for _ in range(world)]
@@ -87,7 +99,8 @@ def _worker(rank, world, port, data, result):
 
 
 @pytest.mark.timeout(120)
-def test_split_kv_exchange_gloo_world2():
+@pytest.mark.parametrize("per_rank", [1, 2])
+def test_split_kv_exchange_gloo_world2(per_rank):
     rng = np.random.default_rng(0)
     hq, hkv, dim, length = 8, 2, 64, 300
     npages = (length + 15) // 16
@@ -101,7 +114,8 @@ def test_split_kv_exchange_gloo_world2():
     manager = ctx.Manager()
     result = manager.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, (q, k, v, pages, length, dim), result))
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, (q, k, v, pages, length, dim, per_rank),
+                                                     result))
              for r in range(2)]
     for p in procs:
         p.start()
