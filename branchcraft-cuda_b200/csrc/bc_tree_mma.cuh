@@ -13,24 +13,33 @@
 //
 // Per 64-token tile:  S = Q K^T  (UMMA 128x64x16, FP16 in, FP32 in TMEM),
 // softmax on S (one thread per row, reads its TMEM lane), P (FP16; FP32-exact
-// output uses P = hi + lo and two MMAs) to shared memory, O += P V (UMMA
-// 128xDx16, V as an MN-major operand) accumulating in TMEM.
+// output uses P = hi + lo and two MMAs) written back over S in TMEM, O += P V
+// (UMMA 128xDx16, V as an MN-major operand) accumulating in TMEM. Q and P are
+// A operands read from tensor memory, so shared memory carries only the K/V
+// tiles: per tile the tensor cores read K once and V once per P part.
 //
 // Warp roles (320 threads): two softmax warpgroups (warps 0-3 and 4-7) take
 // alternate key tiles, each with its own online-softmax state and its own O
 // accumulator in TMEM (thread (w & 3)*32 + lane owns row = TMEM lane of that
-// index); they are merged in the epilogue. Warp 8 is the TMA producer (K/V
-// pages of the page table, draft K/V), warp 9 the TMEM allocator and the
-// single-thread MMA issuer. K/V tiles stream through a 3-stage ring; S/P
-// buffer g belongs to group g, so both groups' softmax overlap each other and
-// the MMAs of their neighbouring tiles.
+// index); they are merged in the epilogue. Warps 8 and 10 are the TMA
+// producers of K and of V (pages of the page table, then draft K/V): the copy
+// rate of paged boxes is bounded per issuing warp, so each ring has its own.
+// Warp 9 is the TMEM allocator and the single-thread MMA issuer. K and V tiles stream through separate rings: a K
+// stage is released as soon as its S = Q K^T has been computed, a V stage once
+// its P V product is done, so the copies of later tiles are not held back by
+// the softmax of earlier ones (5 K stages, 8 V stages). S/P buffer g
+// belongs to group g, so both groups' softmax overlap each other and the MMAs
+// of their neighbouring tiles.
 //
 // The running max is kept lazily: O and l are rescaled only when a row's max
 // grows by more than 2^8 (rare after the first tile), with probabilities up
 // to 2^8 — the final O / l is unchanged.
 //
 // Splits of the key range across the CTAs of a cluster are merged through
-// distributed shared memory, as in bc_attn.cuh.
+// distributed shared memory: the CTAs exchange their per-row (m, l), each
+// scales its own O rows by its share of the final normaliser and stores them
+// into the row's owner CTA (stores need no round trip), and every owner sums
+// its rows' slots in rank order (deterministic) and writes the output.
 #pragma once
 
 #include "bc_attn.cuh"
@@ -39,8 +48,9 @@ namespace bc {
 
 constexpr int kTreeRows = 128;
 constexpr int kTreeTile = 64;        // keys per tile = 4 pages
-constexpr int kTreeStages = 3;
-constexpr int kTreeThreads = 320;   // 8 softmax warps, producer, MMA issuer
+constexpr int kTreeKStages = 5;
+constexpr int kTreeVStages = 8;
+constexpr int kTreeThreads = 352;   // 8 softmax warps, K producer, MMA issuer, V producer
 constexpr int kTreeMaxReq = 128;     // requests per CTA (rows per request >= 1)
 
 struct TreeParams {
@@ -63,28 +73,32 @@ struct TreeParams {
 template <int D, bool PREC>
 struct TreeGeom {
   static constexpr int KB = D / 64;                        // 64-wide swizzle blocks
-  static constexpr int kQBytes = KB * kTreeRows * 128;      // [KB][128 rows][128 B]
+  static constexpr int kKStages = kTreeKStages;
+  static constexpr int kVStages = kTreeVStages;
   static constexpr int kHalfTile = KB * kTreeTile * 128;    // K or V of one tile
-  static constexpr int kStageBytes = 2 * kHalfTile;
-  static constexpr int kPBytes = kTreeRows * kTreeTile * 2;  // one FP16 P tile
-  static constexpr int kPBufBytes = (PREC ? 2 : 1) * kPBytes;
-  static constexpr int kQOff = 0;
-  static constexpr int kKVOff = kQOff + kQBytes;
-  static constexpr int kPOff = kKVOff + kTreeStages * kStageBytes;
-  static constexpr int kBarOff = kPOff + 2 * kPBufBytes;
-  static constexpr int kNumBars = 3 * kTreeStages + 8 + 1;
+  static constexpr int kKOff = 0;
+  static constexpr int kVOff = kKOff + kKStages * kHalfTile;
+  static constexpr int kBarOff = kVOff + kVStages * kHalfTile;
+  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 8 + 1 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   // misc: tmem base (4) + nruns (4) + run tables 6 x kTreeMaxReq ints
   static constexpr int kRunOff = kMiscOff + 16;
   static constexpr int kWg1Off = kRunOff + 6 * kTreeMaxReq * 4;  // [128][2] second group's (m, l)
   static constexpr int kParOff = kWg1Off + kTreeRows * 8;
-  static constexpr int kOStride = D + 4;
-  static_assert(kTreeRows * kOStride * 4 + kTreeRows * 8 <= kTreeStages * kStageBytes,
-                "epilogue buffers must fit in the K/V ring");
+  // Cluster merge (after the main loop, reusing the K/V rings):
+  // kSlotRows received rows [source rank][row] at kKOff, then this CTA's own
+  // 128 weighted rows (16-byte chunks XOR-swizzled by row) at kStageOff.
+  static constexpr int kRowBytes = D * 4;
+  static constexpr int kSlotRows = 136;  // >= csize * ceil(128 / csize), csize <= 8
+  static constexpr int kStageOff = kKOff + kSlotRows * kRowBytes;
+  static_assert(kStageOff + kTreeRows * kRowBytes <= kBarOff,
+                "cluster merge buffers must fit in the K/V rings");
   // parent rows (anc_rows ints, 16-byte padded) then ancestor sets (32 B each)
   __host__ __device__ static size_t anc_offset(int anc_rows) { return size_t(kParOff) + ((size_t(anc_rows) * 4 + 15) & ~size_t(15)); }
   static size_t smem_bytes(int anc_rows) { return 1024 + anc_offset(anc_rows) + size_t(anc_rows) * 32; }
-  static constexpr uint32_t kTmemCols = 512;  // S/P: 2 x 64, O: 2 x D (<= 128 each)
+  // TMEM columns: S/P of group g at 64 g, O of group g at 128 + 128 g, Q at 384.
+  static constexpr uint32_t kTmemO = 128, kTmemQ = 384;
+  static constexpr uint32_t kTmemCols = 512;
 };
 
 template <int D, bool PREC, bool OUT_HALF>
@@ -103,12 +117,15 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::kBarOff);
-  uint64_t* kv_full = bars;
-  uint64_t* kv_empty = bars + kTreeStages;
-  uint64_t* s_full = bars + 2 * kTreeStages;   // [2]
+  uint64_t* k_full = bars;                          // [kKStages]
+  uint64_t* k_empty = k_full + G::kKStages;
+  uint64_t* v_full = k_empty + G::kKStages;         // [kVStages]
+  uint64_t* v_empty = v_full + G::kVStages;
+  uint64_t* s_full = v_empty + G::kVStages;         // [2]
   uint64_t* p_full = s_full + 2;               // [2]
   uint64_t* pv_done = p_full + 2;              // [2]
   uint64_t* mma_done = pv_done + 2;            // [1]
+  uint64_t* recv_done = mma_done + 1;          // [1] cluster merge: rows received
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kMiscOff);
   int* nruns_s = reinterpret_cast<int*>(smem + G::kMiscOff + 4);
   int* run_first = reinterpret_cast<int*>(smem + G::kRunOff);  // first local request
@@ -137,16 +154,73 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   const int nreq = min(p.req_per_block, p.batch - b0);
   const int npad = (p.nodes + 15) & ~15;              // draft slots per request
 
-  // ---- prologue. Every global load of the prologue is issued in one phase
-  // (lengths, parent rows, page-row comparisons, query rows, and the
-  // producer's speculative page ids for a single shared prefix), so the CTA
-  // pays one memory round trip before its first K/V copy.
+  // ---- prologue. Every global load of the prologue (lengths, parent rows,
+  // page-row comparisons, query rows, the producer's speculative page ids) is
+  // issued before any of their results is used, so the CTA pays one memory
+  // round trip before its first K/V copy; barrier set-up and the TMEM
+  // allocation overlap it.
   const int cap = p.max_pages * kPageSize;
   const int ndraft_tiles = (nreq * npad + kTreeTile - 1) / kTreeTile;
+  const int npar = nreq * p.nodes;              // <= 256: R * nodes (host)
+  const int ncmp = (nreq - 1) * p.max_pages;    // page-row comparisons
+  const int ld_len = tid < nreq ? __ldg(p.lengths + b0 + tid) : 0;
+  const int ld_par = tid < npar ? __ldg(p.parent + size_t(b0) * p.nodes + tid) : 0;
+  int cmp_a[4], cmp_b[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int w = tid + k * kTreeThreads;
+    cmp_a[k] = cmp_b[k] = 0;
+    if (w < ncmp) {
+      const int i = 1 + w / p.max_pages, j = w % p.max_pages;
+      cmp_a[k] = __ldg(p.pages + size_t(b0 + i) * p.max_pages + j);
+      cmp_b[k] = __ldg(p.pages + size_t(b0 + i - 1) * p.max_pages + j);
+    }
+  }
+  // Query row r (thread r of warps 0-3) into registers, for TMEM lane r.
+  uint32_t qv[D / 2];
+  if (warp < 4) {
+    const int br = trow * kTreeRows + tid;
+    const bool ok = br < nreq * p.rows_req;
+    const int rq = ok ? br / p.rows_req : 0, node = ok ? (br % p.rows_req) / p.group : 0;
+    const int hh = ok ? br % p.group : 0;
+    const uint4* src = reinterpret_cast<const uint4*>(
+        p.q + ((size_t(b0 + rq) * p.nodes + node) * p.hq + size_t(kvh) * p.group + hh) * D);
+#pragma unroll
+    for (int k = 0; k < D / 8; ++k) {
+      const uint4 v = ok ? __ldg(src + k) : make_uint4(0u, 0u, 0u, 0u);
+      qv[4 * k + 0] = v.x;
+      qv[4 * k + 1] = v.y;
+      qv[4 * k + 2] = v.z;
+      qv[4 * k + 3] = v.w;
+    }
+  }
+  // Producer: page ids of tiles 0..15 of this CTA's key range, speculating
+  // that the block is one run of request b0's prefix spanning the whole page
+  // table; the producer checks the guess after phase 2.
+  const int spec_t0 = (cap + kTreeTile - 1) / kTreeTile;
+  int cur_ids = -1, next_ids = -1;
+  if (warp == 8 || warp == 10) {
+    const int tot = spec_t0 + ndraft_tiles;
+    const int per0 = (tot + p.splits - 1) / p.splits;
+    const int spec_v0 = min(tot, split * per0);
+    auto spec_id = [&](int i) -> int {
+      const int v = spec_v0 + i;
+      if (v >= spec_t0) return -1;
+      const int pg = v * 4 + (lane & 3);
+      if (pg >= p.max_pages) return -1;
+      return __ldg(p.pages + size_t(b0) * p.max_pages + pg);
+    };
+    cur_ids = spec_id(lane >> 2);
+    next_ids = spec_id(8 + (lane >> 2));
+  }
   if (tid == 0) {
-    for (int s = 0; s < kTreeStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < G::kKStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < G::kVStages; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
@@ -154,90 +228,45 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       mbar_init(&pv_done[s], 1);
     }
     mbar_init(mma_done, 1);
+    mbar_init(recv_done, 1);
     fence_mbar_init();
   }
   if (warp == 9) {
     tmem_alloc(tmem_slot, G::kTmemCols);
     tmem_relinquish();
+    tc_fence_before();
   }
   for (int i = tid; i < nreq; i += kTreeThreads) mismatch[i] = 0x7fffffff;
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t lane_addr = uint32_t((warp & 3) * 32) << 16;  // this warp's TMEM lanes
 
-  // Phase 1: loads only.
-  for (int i = tid; i < nreq; i += kTreeThreads) len_s[i] = __ldg(p.lengths + b0 + i);
-  for (int e = tid; e < nreq * p.nodes; e += kTreeThreads)
-    par_s[e] = __ldg(p.parent + size_t(b0) * p.nodes + e);
+  // Phase 1: the loaded values into shared memory.
+  for (int i = tid; i < nreq; i += kTreeThreads)
+    len_s[i] = i == tid ? ld_len : __ldg(p.lengths + b0 + i);
+  for (int e = tid; e < npar; e += kTreeThreads)
+    par_s[e] = e == tid ? ld_par : __ldg(p.parent + size_t(b0) * p.nodes + e);
   // First page where request i's row differs from request i-1's.
-  for (int w0 = tid; w0 < (nreq - 1) * p.max_pages; w0 += 4 * kTreeThreads) {
-    int a[4], bb[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int w = w0 + k * kTreeThreads;
-      a[k] = bb[k] = 0;
-      if (w < (nreq - 1) * p.max_pages) {
-        const int i = 1 + w / p.max_pages, j = w % p.max_pages;
-        a[k] = __ldg(p.pages + size_t(b0 + i) * p.max_pages + j);
-        bb[k] = __ldg(p.pages + size_t(b0 + i - 1) * p.max_pages + j);
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int w = w0 + k * kTreeThreads;
-      if (w < (nreq - 1) * p.max_pages && a[k] != bb[k])
-        atomicMin(&mismatch[1 + w / p.max_pages], w % p.max_pages);
-    }
+  for (int k = 0; k < 4; ++k) {
+    const int w = tid + k * kTreeThreads;
+    if (w < ncmp && cmp_a[k] != cmp_b[k]) atomicMin(&mismatch[1 + w / p.max_pages], w % p.max_pages);
   }
-  {  // query rows -> shared memory (K-major, 128-byte swizzle); all loads of
-     // a thread are issued before its stores.
-    constexpr int kChunks = kTreeRows * (D / 8);
-    constexpr int kPer = (kChunks + kTreeThreads - 1) / kTreeThreads;
-    uint4 v[kPer];
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int c = tid + k * kTreeThreads;
-      v[k] = make_uint4(0u, 0u, 0u, 0u);
-      if (c < kChunks) {
-        const int r = c / (D / 8), chunk = c % (D / 8);
-        const int br = trow * kTreeRows + r;
-        if (br < nreq * p.rows_req) {
-          const int rq = br / p.rows_req, node = (br % p.rows_req) / p.group, hh = br % p.group;
-          v[k] = __ldg(reinterpret_cast<const uint4*>(
-              p.q + ((size_t(b0 + rq) * p.nodes + node) * p.hq + size_t(kvh) * p.group + hh) * D +
-              chunk * 8));
-        }
-      }
-    }
-    uint8_t* qs = smem + G::kQOff;
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int c = tid + k * kTreeThreads;
-      if (c < kChunks) {
-        const int r = c / (D / 8), chunk = c % (D / 8);
-        const int blkq = chunk >> 3, cc = chunk & 7;
-        *reinterpret_cast<uint4*>(qs + blkq * (kTreeRows * 128) + r * 128 + ((cc ^ (r & 7)) << 4)) =
-            v[k];
-      }
-    }
-    fence_proxy_async_smem();
+  for (int w = tid + 4 * kTreeThreads; w < ncmp; w += kTreeThreads) {  // very wide tables only
+    const int i = 1 + w / p.max_pages, j = w % p.max_pages;
+    if (__ldg(p.pages + size_t(b0 + i) * p.max_pages + j) !=
+        __ldg(p.pages + size_t(b0 + i - 1) * p.max_pages + j))
+      atomicMin(&mismatch[i], j);
   }
-  // Producer: speculative page ids of tiles 0..15 of this CTA's range under
-  // the assumption that all requests of the block share request b0's prefix.
-  int spec_len0 = 0, spec_v0 = 0, cur_ids = -1, next_ids = -1;
-  if (warp == 8) {
-    spec_len0 = min(max(__ldg(p.lengths + b0), 0), cap);
-    const int t0 = (spec_len0 + kTreeTile - 1) / kTreeTile;
-    const int tot = t0 + ndraft_tiles;
-    const int per0 = (tot + p.splits - 1) / p.splits;
-    spec_v0 = min(tot, split * per0);
-    auto spec_id = [&](int i) -> int {
-      const int v = spec_v0 + i;
-      if (v >= t0) return -1;
-      const int pg = v * 4 + (lane & 3);
-      if (pg * kPageSize >= spec_len0) return -1;
-      return __ldg(p.pages + size_t(b0) * p.max_pages + pg);
-    };
-    cur_ids = spec_id(lane >> 2);
-    next_ids = spec_id(8 + (lane >> 2));
+  if (warp < 4) {  // query rows -> TMEM (the A operand of S = Q K^T)
+    uint32_t (&q0)[32] = *reinterpret_cast<uint32_t (*)[32]>(&qv[0]);
+    tmem_st32(tbase + lane_addr + G::kTmemQ, q0);
+    if constexpr (D == 128) {
+      uint32_t (&q1)[32] = *reinterpret_cast<uint32_t (*)[32]>(&qv[32]);
+      tmem_st32(tbase + lane_addr + G::kTmemQ + 32, q1);
+    }
+    tmem_st_wait();
   }
   tc_fence_before();
   __syncthreads();
@@ -281,7 +310,6 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   }
   __syncthreads();
   tc_fence_after();
-  const uint32_t tbase = *tmem_slot;
   const int nruns = *nruns_s;
 
   // ---- this CTA's slice of the key tiles: all runs' prefix tiles, then drafts
@@ -302,19 +330,16 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     }
   };
 
-  const uint32_t q_addr = smem_u32(smem + G::kQOff);
-  const uint32_t kv_addr = smem_u32(smem + G::kKVOff);
-  const uint32_t p_addr = smem_u32(smem + G::kPOff);
+  const uint32_t k_addr = smem_u32(smem + G::kKOff);
+  const uint32_t v_addr = smem_u32(smem + G::kVOff);
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ producer
+  if (warp == 8 || warp == 10) {
+    // ------------------------------------------------------------ producers
+    const bool v_warp = warp == 10;
     if (ntiles > 0) {
       int run, t;
       start_cursor(v0, run, t);
-      if (lane == 0) {
-        prefetch_tmap(&kmap);
-        prefetch_tmap(&vmap);
-      }
+      if (lane == 0) prefetch_tmap(v_warp ? &vmap : &kmap);
       // Lane l holds the page id of page (l & 3) of tile (batch*8 + l/4); the
       // next batch is loaded while this one is issued. The prologue's
       // speculative ids stand when the block is one run of request b0.
@@ -328,52 +353,63 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         if (pg * kPageSize >= run_len[rr]) return -1;
         return __ldg(p.pages + size_t(b0 + run_first[rr]) * p.max_pages + pg);
       };
-      if (!(nruns == 1 && spec_v0 == v0)) {
+      if (nruns == 1 && run_tiles[0] == spec_t0) {
+        // The speculation held (one run, as many prefix tiles as the table
+        // width, hence the same key range): mask the pages past the length.
+        auto mask = [&](int id, int first) -> int {
+          const int pg = (v0 + first + (lane >> 2)) * 4 + (lane & 3);
+          return pg * kPageSize >= run_len[0] ? -1 : id;
+        };
+        cur_ids = mask(cur_ids, 0);
+        next_ids = mask(next_ids, 8);
+      } else {
         cur_ids = load_ids(0);
         next_ids = load_ids(8);
       }
-      for (int i = 0; i < ntiles; ++i) {
-        const int stage = i % kTreeStages;
-        if (i >= kTreeStages) {
-          const bool ok = mbar_wait(&kv_empty[stage], ((i / kTreeStages) - 1) & 1);
-          if (!__all_sync(0xffffffffu, ok)) {
-            if (lane == 0) atomicOr(p.err, kErrTimeout);
-            break;
+      // K or V of tile i into its ring; lane 0 posts the expected bytes, then
+      // every box is issued by its own lane.
+      auto issue = [&](int i, bool is_v, bool is_prefix, int page_id) -> bool {
+        const int nst = is_v ? G::kVStages : G::kKStages;
+        const int st = i % nst;
+        uint64_t* full = (is_v ? v_full : k_full) + st;
+        if (i >= nst) {
+          const bool ok = mbar_wait((is_v ? v_empty : k_empty) + st, ((i / nst) - 1) & 1);
+          if (!__all_sync(0xffffffffu, ok)) return false;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(full, uint32_t(G::kHalfTile));
+        __syncwarp();
+        if (lane < 4 * KB) {
+          const int j = lane / KB;   // page of the tile
+          const int kb = lane % KB;  // 64-dim block
+          uint8_t* dst = smem + (is_v ? G::kVOff : G::kKOff) + st * G::kHalfTile +
+                         kb * (kTreeTile * 128) + j * 2048;
+          if (is_prefix) {
+            tma_load_4d(dst, is_v ? &vmap : &kmap, full, kb * 64, kvh, 0, page_id);
+          } else {
+            const int slot = (t * 4 + j) * 16;  // draft slot of this box
+            const int rq = slot / npad, nb = slot % npad;
+            const int b = rq < nreq ? b0 + rq : p.batch;  // past the block: zeros
+            tma_load_4d(dst, is_v ? &dvmap : &dkmap, full, kb * 64, kvh, nb, b);
           }
         }
+        __syncwarp();
+        return true;
+      };
+      for (int i = 0; i < ntiles; ++i) {
         if (i > 0 && (i & 7) == 0) {
           cur_ids = next_ids;
           next_ids = load_ids(i + 8);
         }
         const bool is_prefix = run < nruns;
-        int ids[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) ids[j] = __shfl_sync(0xffffffffu, cur_ids, (i & 7) * 4 + j);
-        if (lane == 0 && is_prefix)
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (ids[j] >= p.physical_pages || ids[j] < -1) atomicOr(p.err, kErrPageRange);
-        // Lane 0 posts the expected bytes, then every box of the tile is
-        // issued by its own lane: a single issuing thread caps the copy rate
-        // of the CTA well below what the tensor cores consume.
-        uint8_t* kdst = smem + G::kKVOff + stage * G::kStageBytes;
-        if (lane == 0) mbar_arrive_expect_tx(&kv_full[stage], uint32_t(G::kStageBytes));
-        __syncwarp();
-        if (lane < 4 * KB * 2) {
-          const int j = lane / (KB * 2);         // page of the tile
-          const int kb = (lane >> 1) % KB;       // 64-dim half
-          const bool is_v = lane & 1;
-          uint8_t* dst = kdst + (is_v ? G::kHalfTile : 0) + kb * (kTreeTile * 128) + j * 2048;
-          if (is_prefix) {
-            tma_load_4d(dst, is_v ? &vmap : &kmap, &kv_full[stage], kb * 64, kvh, 0, ids[j]);
-          } else {
-            const int slot = (t * 4 + j) * 16;  // draft slot of this box
-            const int rq = slot / npad, nb = slot % npad;
-            const int b = rq < nreq ? b0 + rq : p.batch;  // past the block: zeros
-            tma_load_4d(dst, is_v ? &dvmap : &dkmap, &kv_full[stage], kb * 64, kvh, nb, b);
-          }
+        // the page id of this lane's box (page lane / KB of the tile)
+        const int page_id = __shfl_sync(0xffffffffu, cur_ids, (i & 7) * 4 + min(lane / KB, 3));
+        if (!v_warp && is_prefix && lane < 4 * KB && lane % KB == 0 &&
+            (page_id >= p.physical_pages || page_id < -1))
+          atomicOr(p.err, kErrPageRange);
+        if (!issue(i, v_warp, is_prefix, page_id)) {
+          if (lane == 0) atomicOr(p.err, kErrTimeout);
+          break;
         }
-        __syncwarp();
         ++t;
         while (run < nruns && t >= run_tiles[run]) {  // empty runs have no tiles
           t -= run_tiles[run];
@@ -385,47 +421,45 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (ntiles > 0 && lane == 0) {
       bool ok = true;
-      const uint32_t tS[2] = {tbase, tbase + 64};
       auto issue_pv = [&](int i) {
-        const int stage = i % kTreeStages;
+        const int vst = i % G::kVStages;
         const int buf = i & 1;
         if (!mbar_wait(&p_full[buf], (i >> 1) & 1)) return false;
+        if (!mbar_wait(&v_full[vst], (i / G::kVStages) & 1)) return false;
         tc_fence_after();
-        const uint32_t vbase = kv_addr + stage * G::kStageBytes + G::kHalfTile;
-        const uint32_t pbase = p_addr + buf * G::kPBufBytes;
-        const uint32_t tO = tbase + 128 + buf * 128;  // group buf's accumulator
+        const uint32_t vbase = v_addr + vst * G::kHalfTile;
+        const uint32_t tP = tbase + uint32_t(buf) * 64;           // P hi (+32: lo)
+        const uint32_t tO = tbase + G::kTmemO + uint32_t(buf) * 128;  // group buf's O
 #pragma unroll
         for (int kk = 0; kk < kTreeTile / 16; ++kk) {
           // V: MN-major (dims contiguous); 16 keys = two 8-key groups 1024 B apart;
-          // the second 64-dim block sits kTreeTile*128 bytes further.
+          // the second 64-dim block sits kTreeTile*128 bytes further. P: 16 keys
+          // = 8 TMEM columns of FP16 pairs.
           const uint64_t bdesc = umma_desc_sw128(vbase + kk * 2048, kTreeTile * 128, 1024);
-          const uint64_t adesc = umma_desc_sw128(pbase + kk * 32, 16, 1024);
-          umma_f16(tO, adesc, bdesc, kIdescPV, (i >= 2 || kk > 0) ? 1u : 0u);
-          if (PREC) {
-            const uint64_t ldesc = umma_desc_sw128(pbase + G::kPBytes + kk * 32, 16, 1024);
-            umma_f16(tO, ldesc, bdesc, kIdescPV, 1u);
-          }
+          umma_f16_ts(tO, tP + kk * 8, bdesc, kIdescPV, (i >= 2 || kk > 0) ? 1u : 0u);
+          if (PREC) umma_f16_ts(tO, tP + 32 + kk * 8, bdesc, kIdescPV, 1u);
         }
         umma_commit(&pv_done[buf]);
-        umma_commit(&kv_empty[stage]);
+        umma_commit(&v_empty[vst]);
         return true;
       };
       for (int i = 0; i < ntiles && ok; ++i) {
-        const int stage = i % kTreeStages;
-        if (!mbar_wait(&kv_full[stage], (i / kTreeStages) & 1)) {
+        const int kst = i % G::kKStages;
+        if (!mbar_wait(&k_full[kst], (i / G::kKStages) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t kbase = kv_addr + stage * G::kStageBytes;
+        const uint32_t kbase = k_addr + kst * G::kHalfTile;
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const int kb = ks >> 2, kin = ks & 3;
-          const uint64_t adesc = umma_desc_sw128(q_addr + kb * (kTreeRows * 128) + kin * 32, 16, 1024);
           const uint64_t bdesc = umma_desc_sw128(kbase + kb * (kTreeTile * 128) + kin * 32, 16, 1024);
-          umma_f16(tS[i & 1], adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
+          umma_f16_ts(tbase + uint32_t(i & 1) * 64, tbase + G::kTmemQ + ks * 8, bdesc, kIdescS,
+                      ks > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[i & 1]);
+        umma_commit(&k_empty[kst]);  // K stage free once S is computed
         if (i > 0) ok = issue_pv(i - 1);
       }
       if (ok) ok = issue_pv(ntiles - 1);
@@ -443,8 +477,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   const bool row_valid = warp < 8 && brow < nreq * p.rows_req;
   const int my_req = row_valid ? brow / p.rows_req : -1;
   const int my_node = row_valid ? (brow % p.rows_req) / p.group : 0;
-  const uint32_t lane_addr = uint32_t((warp & 3) * 32) << 16;
-  const uint32_t o_col = 128 + uint32_t(wg & 1) * 128;  // this group's O in TMEM
+  const uint32_t o_col = G::kTmemO + uint32_t(wg & 1) * 128;  // this group's O in TMEM
   bool softmax_ok = true;
   if (warp < 8 && ntiles > wg) {
     int run, t;
@@ -518,20 +551,23 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         l_sum *= alpha;
       }
       const float mb = m_ref == kNegInf ? 0.f : m_ref;
-      // P tile buffer `buf` is free once PV of tile i-2 is done.
+      // This group's O is free for the rescale once PV of tile i-2 is done
+      // (already implied by S(i) being complete: the MMAs run in issue order).
       if (i >= 2 && !mbar_wait(&pv_done[buf], ((i - 2) >> 1) & 1)) {
         softmax_ok = false;
         break;
       }
-      uint8_t* prow = smem + G::kPOff + buf * G::kPBufBytes + r * 128;
+      // P over S's own TMEM columns: hi at +0, lo at +32 (FP16 pairs), in
+      // two halves of 32 keys to bound the live registers.
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 64; c += 8) {
-        uint32_t hi[4], lo[4];
+      for (int half = 0; half < 2; ++half) {
+        uint32_t ph[16], pl[16];
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const float p0 = fast_exp2(fmaf(x[c + e], p.scale_log2, -mb));
-          const float p1 = fast_exp2(fmaf(x[c + e + 1], p.scale_log2, -mb));
+        for (int e = 0; e < 32; e += 2) {
+          const int c = half * 32 + e;
+          const float p0 = fast_exp2(fmaf(x[c], p.scale_log2, -mb));
+          const float p1 = fast_exp2(fmaf(x[c + 1], p.scale_log2, -mb));
           ls[(e >> 1) & 3] += p0 + p1;
           if (PREC) {
             // Veltkamp split: h = p rounded to 11 significant bits (exact in
@@ -541,23 +577,26 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
             const float t0 = __fmul_rn(p0, 8193.f), t1 = __fmul_rn(p1, 8193.f);
             const float h0 = __fsub_rn(t0, __fsub_rn(t0, p0));
             const float h1 = __fsub_rn(t1, __fsub_rn(t1, p1));
-            hi[e / 2] = pack_half2(h0, h1);
-            lo[e / 2] = pack_half2(__fsub_rn(p0, h0), __fsub_rn(p1, h1));
+            ph[e / 2] = pack_half2(h0, h1);
+            pl[e / 2] = pack_half2(__fsub_rn(p0, h0), __fsub_rn(p1, h1));
           } else {
-            hi[e / 2] = pack_half2(p0, p1);
+            ph[e / 2] = pack_half2(p0, p1);
           }
         }
-        const int chunk = c >> 3;
-        uint8_t* a = prow + ((chunk ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(a) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        if (PREC) *reinterpret_cast<uint4*>(a + G::kPBytes) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        tmem_st16(tbase + lane_addr + uint32_t(buf) * 64 + half * 16, ph);
+        if (PREC) tmem_st16(tbase + lane_addr + uint32_t(buf) * 64 + 32 + half * 16, pl);
       }
       l_sum += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // Keys past a prefix run's end may hold anything: zero their V rows so
       // that 0 * V stays 0 in the PV product.
       if (is_prefix && valid_keys < kTreeTile) {
-        const int stage = i % kTreeStages;
-        const uint32_t vbase = kv_addr + stage * G::kStageBytes + G::kHalfTile;
+        // (the V tile may still be in flight: wait for it before writing)
+        const int vst = i % G::kVStages;
+        if (!mbar_wait(&v_full[vst], (i / G::kVStages) & 1)) {
+          softmax_ok = false;
+          break;
+        }
+        const uint32_t vbase = v_addr + vst * G::kHalfTile;
         const int rows_bad = kTreeTile - valid_keys;
         for (int c = r; c < rows_bad * KB * 8; c += 128) {
           const int key = valid_keys + c / (KB * 8);
@@ -565,8 +604,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           const int kb = rem >> 3, ch = rem & 7;
           st_shared_v4(vbase + kb * (kTreeTile * 128) + key * 128 + (ch << 4), 0u, 0u, 0u, 0u);
         }
+        fence_proxy_async_smem();
       }
-      fence_proxy_async_smem();
       // O rescale (whole warp when any of its rows needs it). This group's
       // previous PV (tile i-2) is complete: it was waited for above.
       if (__any_sync(0xffffffffu, rescale)) {
@@ -581,8 +620,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
           tmem_st32(tbase + lane_addr + o_col + c, o);
         }
-        tmem_st_wait();
       }
+      tmem_st_wait();  // P (and a rescaled O) are in TMEM before the MMA reads them
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[buf]);
@@ -596,18 +635,29 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   }
 
   // ------------------------------------------------------------ epilogue
-  // Wait for the last PV, then each row thread reads its O row.
+  // Wait for the last PV, then each row thread of group 0 reads its O rows.
   const bool to_cluster = p.splits > 1;
-  using TG = TreeGeom<D, PREC>;
-  float* fo = reinterpret_cast<float*>(smem + G::kKVOff);          // [128][D+4]
-  float* fml = fo + kTreeRows * TG::kOStride;                       // [128][2]
+  const int csize = p.splits;
+  const uint32_t rank = to_cluster ? cluster_ctarank() : 0u;
+  const int rpk = (kTreeRows + csize - 1) / csize;  // rows owned by each CTA of the cluster
+  const int valid_rows = min(kTreeRows, nreq * p.rows_req - trow * kTreeRows);
   auto out_ptr = [&](int row) -> size_t {
     const int br = trow * kTreeRows + row;
     const int rq = br / p.rows_req, node = (br % p.rows_req) / p.group, hh = br % p.group;
     return ((size_t(b0 + rq) * p.nodes + node) * p.hq + size_t(kvh) * p.group + hh) * D;
   };
-  // Group 1 hands its (m, l) to group 0 through shared memory; group 0 merges
-  // the two O accumulators row by row.
+  auto store_out4 = [&](size_t base, float a, float b, float c, float d) {
+    if constexpr (OUT_HALF) {
+      uint2 v;
+      v.x = pack_half2(a, b);
+      v.y = pack_half2(c, d);
+      *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.out) + base) = v;
+    } else {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base) = make_float4(a, b, c, d);
+    }
+  };
+  // Group 1 hands its (m, l) to group 0 through shared memory; group 0 then
+  // publishes the CTA's (m, l) per row in the same place for the cluster.
   float* wg1_ml = reinterpret_cast<float*>(smem + G::kWg1Off);
   bool have = false;
   if (warp < 8) {
@@ -623,65 +673,91 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     }
     named_barrier_sync(2, 256);
   }
+  // Weights of the two groups' accumulators: final O = w0 * O0 + w1 * O1.
+  float w0 = 0.f, w1 = 0.f, mm = kNegInf;
+  bool use0 = false, use1 = false;
   if (warp < 4) {
-    tc_fence_after();
     const float m1 = wg1_ml[r * 2 + 0], l1 = wg1_ml[r * 2 + 1];
     const float m0 = have ? m_ref : kNegInf, l0 = have ? l_sum : 0.f;
-    const float mm = fmaxf(m0, m1);
-    // Per row: a group contributes only if its max is finite. The TMEM reads
-    // themselves are warp-collective, so they depend only on whether the
-    // group processed any tile at all (uniform across the warp).
-    const bool use0 = m0 != kNegInf, use1 = m1 != kNegInf;
-    const float w0 = use0 ? fast_exp2(m0 - mm) : 0.f;
-    const float w1 = use1 ? fast_exp2(m1 - mm) : 0.f;
+    mm = fmaxf(m0, m1);
+    // A group contributes only if its max is finite (it saw a valid key).
+    use0 = m0 != kNegInf;
+    use1 = m1 != kNegInf;
+    w0 = use0 ? fast_exp2(m0 - mm) : 0.f;
+    w1 = use1 ? fast_exp2(m1 - mm) : 0.f;
     const float lsum = w0 * l0 + w1 * l1;
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    if (to_cluster) {
+      wg1_ml[r * 2 + 0] = mm;
+      wg1_ml[r * 2 + 1] = lsum;
+    } else {
+      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+      w0 *= inv;
+      w1 *= inv;
+    }
+  }
+  // Rows of this tile owned by this CTA in the cluster merge.
+  const int own_rows = to_cluster ? max(0, min(rpk, valid_rows - int(rank) * rpk)) : 0;
+  if (to_cluster && tid == 0 && own_rows > 0)  // armed before any peer can send
+    mbar_arrive_expect_tx(recv_done, uint32_t((csize - 1) * own_rows * G::kRowBytes));
+  if (to_cluster) {
+    cluster_sync_all();  // every CTA's (m, l) is final and its rings are idle
+    if (warp < 4 && r < valid_rows) {
+      const uint32_t ml_addr = smem_u32(wg1_ml + r * 2);
+      float2 mlc[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        if (c < csize) mlc[c] = ld_cluster_f32x2(map_to_rank(ml_addr, uint32_t(c)));
+      float M = kNegInf;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        if (c < csize) M = fmaxf(M, mlc[c].x);
+      float L = 0.f;
+      if (M != kNegInf) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          if (c < csize && mlc[c].x != kNegInf) L += fast_exp2(mlc[c].x - M) * mlc[c].y;
+      }
+      // This CTA's share of the row: exp2(mm - M) / L (0 for a CTA without keys).
+      const float share = (mm != kNegInf && L > 0.f) ? fast_exp2(mm - M) / L : 0.f;
+      w0 *= share;
+      w1 *= share;
+    }
+  }
+  if (warp < 4) {
+    tc_fence_after();
+    // The TMEM reads are warp-collective: they depend only on whether the
+    // group processed any tile at all (uniform across the warp).
     const bool read0 = ntiles > 0, read1 = ntiles > 1;
+    uint8_t* srow = smem + G::kStageOff + r * G::kRowBytes;
 #pragma unroll 1
     for (int c = 0; c < D; c += 32) {
       uint32_t o[32], o1[32];
-      if (read0) tmem_ld32(tbase + lane_addr + 128 + c, o);
-      if (read1) tmem_ld32(tbase + lane_addr + 256 + c, o1);
+      if (read0) tmem_ld32(tbase + lane_addr + G::kTmemO + c, o);
+      if (read1) tmem_ld32(tbase + lane_addr + G::kTmemO + 128 + c, o1);
       tmem_ld_wait();
+      float f[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const float a = (read0 && use0) ? w0 * __uint_as_float(o[e]) : 0.f;
         const float b = (read1 && use1) ? w1 * __uint_as_float(o1[e]) : 0.f;
-        o[e] = __float_as_uint(a + b);
+        f[e] = a + b;
       }
-      if (to_cluster) {
+      if (r < valid_rows) {
+        if (to_cluster) {
 #pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          *reinterpret_cast<float4*>(fo + r * TG::kOStride + c + e) =
-              make_float4(__uint_as_float(o[e]), __uint_as_float(o[e + 1]),
-                          __uint_as_float(o[e + 2]), __uint_as_float(o[e + 3]));
-      } else if (row_valid) {
-        const size_t base = out_ptr(r) + c;
-        if constexpr (OUT_HALF) {
-          __half* dst = reinterpret_cast<__half*>(p.out) + base;
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 v;
-            v.x = pack_half2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
-            v.y = pack_half2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
-            v.z = pack_half2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
-            v.w = pack_half2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + e) = v;
+          for (int e = 0; e < 32; e += 4) {
+            const int chunk = (c + e) >> 2;
+            *reinterpret_cast<float4*>(srow + ((chunk ^ (r & 7)) << 4)) =
+                make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
           }
         } else {
-          float* dst = reinterpret_cast<float*>(p.out) + base;
+          const size_t base = out_ptr(r) + c;
 #pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            *reinterpret_cast<float4*>(dst + e) =
-                make_float4(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv,
-                            __uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+          for (int e = 0; e < 32; e += 4) store_out4(base + e, f[e], f[e + 1], f[e + 2], f[e + 3]);
         }
       }
     }
-    if (to_cluster) {
-      fml[r * 2 + 0] = mm;
-      fml[r * 2 + 1] = lsum;
-    }
+    if (to_cluster) fence_proxy_async_smem();  // staged rows -> the bulk copies
   }
   tc_fence_before();
   __syncthreads();
@@ -689,63 +765,46 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     tc_fence_after();
     tmem_dealloc(tbase, G::kTmemCols);
   }
-
   if (to_cluster) {
-    // Merge the key splits of this row tile across the cluster (DSMEM).
-    __syncwarp();
-    cluster_sync_all();
-    const uint32_t rank = cluster_ctarank();
-    const int csize = p.splits;
-    const uint32_t fo_addr = smem_u32(fo), fml_addr = smem_u32(fml);
-    // Only rows that exist are merged: tasks cover valid_rows x D/4 quads.
-    const int valid_rows = min(kTreeRows, nreq * p.rows_req - trow * kTreeRows);
-    const int quads = valid_rows * (D / 4);
-    for (int task = int(rank) * kTreeThreads + tid; task < quads;
-         task += csize * kTreeThreads) {
-      const int row = task / (D / 4), d4 = (task % (D / 4)) * 4;
-      float mc[8], lc[8];
-      float4 oc[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        if (c < csize) {
-          const float2 ml = ld_cluster_f32x2(map_to_rank(fml_addr + row * 8, c));
-          mc[c] = ml.x;
-          lc[c] = ml.y;
-          oc[c] = ld_cluster_f32x4(map_to_rank(fo_addr + (row * TG::kOStride + d4) * 4, c));
-        }
-      }
-      float mmax = kNegInf;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        if (c < csize) mmax = fmaxf(mmax, mc[c]);
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      float lsum = 0.f;
-      if (mmax != kNegInf) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          if (c < csize) {
-            const float wt = fast_exp2(mc[c] - mmax);
-            lsum += wt * lc[c];
-            acc.x += wt * oc[c].x;
-            acc.y += wt * oc[c].y;
-            acc.z += wt * oc[c].z;
-            acc.w += wt * oc[c].w;
-          }
-        }
-      }
-      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-      const size_t base = out_ptr(row) + d4;
-      if constexpr (OUT_HALF) {
-        uint2 v;
-        v.x = pack_half2(acc.x * inv, acc.y * inv);
-        v.y = pack_half2(acc.z * inv, acc.w * inv);
-        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.out) + base) = v;
-      } else {
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base) =
-            make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    // Send every peer the rows it owns (one bulk copy each, completing on
+    // the peer's barrier), then sum the received slots of this CTA's own rows
+    // in rank order and store them.
+    if (tid == 0) {
+      for (int k = 0; k < csize; ++k) {
+        const int rows_k = min(rpk, valid_rows - k * rpk);
+        if (k == int(rank) || rows_k <= 0) continue;
+        bulk_copy_to_peer(
+            map_to_rank(smem_u32(smem + G::kKOff) + uint32_t(int(rank) * rpk * G::kRowBytes),
+                        uint32_t(k)),
+            smem_u32(smem + G::kStageOff + k * rpk * G::kRowBytes),
+            uint32_t(rows_k * G::kRowBytes), map_to_rank(smem_u32(recv_done), uint32_t(k)));
       }
     }
-    cluster_sync_all();
+    bool got = true;
+    if (own_rows > 0) got = mbar_wait(recv_done, 0);
+    if (!got) {
+      if (tid == 0) atomicOr(p.err, kErrTimeout);
+    } else {
+      const int row0 = int(rank) * rpk;
+      for (int task = tid; task < own_rows * (D / 4); task += kTreeThreads) {
+        const int rl = task / (D / 4), chunk = task % (D / 4);
+        const int row = row0 + rl;
+        const int off = ((chunk ^ (row & 7)) << 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = 0; c < csize; ++c) {
+          const uint8_t* src = c == int(rank)
+                                   ? smem + G::kStageOff + row * G::kRowBytes
+                                   : smem + G::kKOff + (c * rpk + rl) * G::kRowBytes;
+          const float4 v = *reinterpret_cast<const float4*>(src + off);
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+        store_out4(out_ptr(row) + chunk * 4, acc.x, acc.y, acc.z, acc.w);
+      }
+    }
+    cluster_sync_all();  // no CTA leaves while its rows may still be read or sent
   }
 }
 

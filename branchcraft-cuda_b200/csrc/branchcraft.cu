@@ -283,8 +283,8 @@ cudaError_t configure_tree_kernel(int dev) {
 // CTA per SM at this shared-memory size); cached per device and size.
 template <int D, bool PREC, bool OUT_HALF>
 int tree_max_clusters(int dev, int c) {
-  static std::atomic<int> cache[kMaxDevices][4];
-  const int slot = c == 1 ? 0 : c == 2 ? 1 : c == 4 ? 2 : 3;
+  static std::atomic<int> cache[kMaxDevices][9];
+  const int slot = c;  // 1..8
   int n = cache[dev][slot].load(std::memory_order_relaxed);
   if (n > 0) return n;
   cudaLaunchConfig_t cfg = {};
@@ -309,15 +309,16 @@ int tree_max_clusters(int dev, int c) {
   return n;
 }
 
-// Cluster split along the keys: fill the SMs, stay within one wave of
-// resident clusters, keep at least two key tiles per CTA.
+// Cluster split along the keys: the largest size (any of 1..8) whose CTAs fit
+// on the SMs in one wave of resident clusters, with at least two key tiles per
+// CTA. A small batch needs every SM it can get: each CTA's copy rate, not the
+// memory, bounds it.
 template <int D, bool PREC, bool OUT_HALF>
 int tree_splits(int dev, long long items, int tiles) {
   const int sms = sm_count(dev);
-  int c = 1;
-  while (c < 8 && items * c < sms) c *= 2;
-  while (c > 1 && items > tree_max_clusters<D, PREC, OUT_HALF>(dev, c)) c /= 2;
-  while (c > 1 && (tiles + c - 1) / c < 2) c /= 2;
+  int c = int(std::min<long long>(8, std::max<long long>(1, sms / std::max<long long>(items, 1))));
+  while (c > 1 && (items > tree_max_clusters<D, PREC, OUT_HALF>(dev, c) || (tiles + c - 1) / c < 2))
+    --c;
   return c;
 }
 
