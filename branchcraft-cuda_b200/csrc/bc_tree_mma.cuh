@@ -84,7 +84,8 @@ struct TreeGeom {
   // misc: tmem base (4) + nruns (4) + run tables 6 x kTreeMaxReq ints
   static constexpr int kRunOff = kMiscOff + 16;
   static constexpr int kWg1Off = kRunOff + 6 * kTreeMaxReq * 4;  // [128][2] second group's (m, l)
-  static constexpr int kParOff = kWg1Off + kTreeRows * 8;
+  static constexpr int kORowOff = kWg1Off + kTreeRows * 8;  // [128] output row of each tile row
+  static constexpr int kParOff = kORowOff + kTreeRows * 4;
   // Cluster merge (after the main loop, reusing the K/V rings):
   // kSlotRows received rows [source rank][row] at kKOff, then this CTA's own
   // 128 weighted rows (16-byte chunks XOR-swizzled by row) at kStageOff.
@@ -659,6 +660,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // Group 1 hands its (m, l) to group 0 through shared memory; group 0 then
   // publishes the CTA's (m, l) per row in the same place for the cluster.
   float* wg1_ml = reinterpret_cast<float*>(smem + G::kWg1Off);
+  int* orow = reinterpret_cast<int*>(smem + G::kORowOff);
   bool have = false;
   if (warp < 8) {
     have = ntiles > wg && softmax_ok;
@@ -729,6 +731,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     // group processed any tile at all (uniform across the warp).
     const bool read0 = ntiles > 0, read1 = ntiles > 1;
     uint8_t* srow = smem + G::kStageOff + r * G::kRowBytes;
+    const size_t obase = r < valid_rows ? out_ptr(r) : 0;
+    if (to_cluster) orow[r] = int(obase / D);
 #pragma unroll 1
     for (int c = 0; c < D; c += 32) {
       uint32_t o[32], o1[32];
@@ -751,9 +755,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
                 make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
           }
         } else {
-          const size_t base = out_ptr(r) + c;
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) store_out4(base + e, f[e], f[e + 1], f[e + 2], f[e + 3]);
+          for (int e = 0; e < 32; e += 4) store_out4(obase + c + e, f[e], f[e + 1], f[e + 2], f[e + 3]);
         }
       }
     }
@@ -769,19 +772,23 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     // Send every peer the rows it owns (one bulk copy each, completing on
     // the peer's barrier), then sum the received slots of this CTA's own rows
     // in rank order and store them.
-    if (tid == 0) {
-      for (int k = 0; k < csize; ++k) {
-        const int rows_k = min(rpk, valid_rows - k * rpk);
-        if (k == int(rank) || rows_k <= 0) continue;
+    // (warp k sends peer k's rows: copies issued by different warps proceed
+    // in parallel)
+    if (lane == 0 && warp < csize && warp != int(rank)) {
+      const int k = warp;
+      const int rows_k = min(rpk, valid_rows - k * rpk);
+      if (rows_k > 0)
         bulk_copy_to_peer(
             map_to_rank(smem_u32(smem + G::kKOff) + uint32_t(int(rank) * rpk * G::kRowBytes),
                         uint32_t(k)),
             smem_u32(smem + G::kStageOff + k * rpk * G::kRowBytes),
             uint32_t(rows_k * G::kRowBytes), map_to_rank(smem_u32(recv_done), uint32_t(k)));
-      }
     }
     bool got = true;
     if (own_rows > 0) got = mbar_wait(recv_done, 0);
+    // Every row this CTA owns has arrived, so every copy into it is done:
+    // announce that now, and wait for the peers only before leaving.
+    cluster_arrive_relaxed();
     if (!got) {
       if (tid == 0) atomicOr(p.err, kErrTimeout);
     } else {
@@ -801,10 +808,10 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           acc.z += v.z;
           acc.w += v.w;
         }
-        store_out4(out_ptr(row) + chunk * 4, acc.x, acc.y, acc.z, acc.w);
+        store_out4(size_t(orow[row]) * D + chunk * 4, acc.x, acc.y, acc.z, acc.w);
       }
     }
-    cluster_sync_all();  // no CTA leaves while its rows may still be read or sent
+    cluster_wait();  // no CTA leaves while its staged rows may still be read
   }
 }
 
