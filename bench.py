@@ -54,6 +54,18 @@ PEAKS = ROOT / "MEASURED_PEAKS.json"
 FLUSH_BYTES = 256 << 20
 SCALE = 1.0 / math.sqrt(128.0)
 
+# DRAM bytes per launch of each workload's dominant kernel (dram__bytes_read.sum
+# + dram__bytes_write.sum) from one ncu capture of `python bench.py --workload W
+# --steps 1..3 --warmup 3 --no-cpu-baseline` on a B200. `packed` was captured at
+# --batch 64 (266,106 tokens) and is scaled by tokens to the 256-request batch
+# (1,142,306 tokens): its traffic is a per-token stream.
+NCU_TRAFFIC = {
+    "tree-cow": 9165824,
+    "tree-scale": 1879312128 + 514643968,
+    "decode": 2147777536 + 7383040,
+    "packed": round((1092800512 + 7438080) * 1142306 / 266106),
+}
+
 
 def load_peaks():
     try:
@@ -830,7 +842,9 @@ def run_ours(args):
                 "peak_source": f"{peak_kind} hbm_gbs"}
     roof["kernel"] = wl.kernel
     roof["kernel_us"] = round(kern_us, 3)
-    roof["traffic"] = args.traffic
+    default_shape = not (args.batch or args.context or args.splits)
+    roof["traffic"] = (args.traffic if args.traffic is not None or not default_shape
+                       else NCU_TRAFFIC.get(wl.name))
     h2d, d2h = wl.io_bytes()
     cfg = wl.config()
     cfg["l2"] = ("flushed between timed steps (256 MiB device write, outside the step events)"

@@ -18,7 +18,7 @@
 // A operands read from tensor memory, so shared memory carries only the K/V
 // tiles: per tile the tensor cores read K once and V once per P part.
 //
-// Warp roles (320 threads): two softmax warpgroups (warps 0-3 and 4-7) take
+// Warp roles (352 threads): two softmax warpgroups (warps 0-3 and 4-7) take
 // alternate key tiles, each with its own online-softmax state and its own O
 // accumulator in TMEM (thread (w & 3)*32 + lane owns row = TMEM lane of that
 // index); they are merged in the epilogue. Warps 8 and 10 are the TMA
