@@ -23,6 +23,8 @@ __global__ void __launch_bounds__(256)
                   const int* __restrict__ req, const int* __restrict__ path,
                   const int* __restrict__ dest_pages, const int* __restrict__ dest_slots,
                   int request, unsigned* err) {
+  grid_dependency_wait();  // the preceding kernel of the stream has finished
+  grid_launch_dependents();
   const int e = blockIdx.x;
   const int r = req ? req[e] : request;
   const int node = path[e];
@@ -59,6 +61,8 @@ __global__ void __launch_bounds__(256)
     clone_kernel(int page_halves, int physical_pages, __half* cache_k, __half* cache_v,
                  const int* __restrict__ src_pages, const int* __restrict__ dst_pages,
                  unsigned* err) {
+  grid_dependency_wait();
+  grid_launch_dependents();
   const int c = blockIdx.y;
   const int src = src_pages[c], dst = dst_pages[c];
   if (src < 0 || src >= physical_pages || dst < 0 || dst >= physical_pages) {

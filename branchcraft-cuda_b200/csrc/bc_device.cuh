@@ -75,6 +75,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// ------------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// its predecessor in the stream is still running: it must wait here before
+// touching memory the predecessor writes or reads. No-ops otherwise.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next kernel of the stream (if launched as a programmatic
+// dependent) be scheduled now; it still waits for this grid to finish before
+// its own grid_dependency_wait() returns.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ----------------------------------------------------------------------- TMA
 // 4-D tiled tensor load into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,

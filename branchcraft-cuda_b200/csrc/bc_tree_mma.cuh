@@ -154,6 +154,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   const int b0 = blk * p.req_per_block;
   const int nreq = min(p.req_per_block, p.batch - b0);
   const int npad = (p.nodes + 15) & ~15;              // draft slots per request
+  grid_dependency_wait();  // inputs written by the preceding kernel are visible
 
   // ---- prologue. Every global load of the prologue (lengths, parent rows,
   // page-row comparisons, query rows, the producer's speculative page ids) is
@@ -636,6 +637,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   }
 
   // ------------------------------------------------------------ epilogue
+  // The next kernel of the stream may be scheduled (it waits for this grid).
+  grid_launch_dependents();
   // Wait for the last PV, then each row thread of group 0 reads its O rows.
   const bool to_cluster = p.splits > 1;
   const int csize = p.splits;

@@ -336,14 +336,19 @@ cudaError_t launch_tree_t(TreeParams& p, const CUtensorMap* maps, int items, int
   cfg.blockDim = dim3(kTreeThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  // Programmatic dependent launch: the CTAs may be scheduled while the
+  // preceding kernel finishes; they wait for it before their first load.
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (p.splits > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = unsigned(p.splits);
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = unsigned(p.splits);
+    cfg.numAttrs = 2;
   }
   return cudaLaunchKernelEx(&cfg, kern, p, maps[0], maps[1], maps[2], maps[3]);
 }
@@ -586,19 +591,32 @@ int bc_commit_batch(const bc_shape* s, int nodes, const void* draft_k, const voi
   if (!err) return cudaErrorInvalidDevice;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int row = s->kv_heads * s->dim;
+  // Both launches are programmatic dependents of the kernel before them: the
+  // clones wait for the preceding kernel, the row writes for the clones.
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = st;
+  cfg.attrs = pdl;
+  cfg.numAttrs = 1;
   if (nclones > 0) {
-    clone_kernel<<<dim3(4, unsigned(nclones), 2), 256, 0, st>>>(
-        16 * row, s->physical_pages, static_cast<__half*>(cache_k), static_cast<__half*>(cache_v),
-        clone_src, clone_dst, err);
-    cudaError_t e = cudaGetLastError();
+    cfg.gridDim = dim3(4, unsigned(nclones), 2);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, clone_kernel, 16 * row, s->physical_pages,
+                                       static_cast<__half*>(cache_k),
+                                       static_cast<__half*>(cache_v), clone_src, clone_dst, err);
     if (e != cudaSuccess) return e;
   }
-  if (nentries > 0)
-    commit_kernel<true><<<nentries, 256, 0, st>>>(
-        row, s->batch, nodes, s->physical_pages, static_cast<const __half*>(draft_k),
-        static_cast<const __half*>(draft_v), static_cast<__half*>(cache_k),
-        static_cast<__half*>(cache_v), entry_request, entry_node, entry_page, entry_slot, 0, err);
-  return cudaGetLastError();
+  if (nentries > 0) {
+    cfg.gridDim = dim3(unsigned(nentries), 1, 1);
+    return cudaLaunchKernelEx(&cfg, commit_kernel<true>, row, s->batch, nodes,
+                              s->physical_pages, static_cast<const __half*>(draft_k),
+                              static_cast<const __half*>(draft_v), static_cast<__half*>(cache_k),
+                              static_cast<__half*>(cache_v), entry_request, entry_node,
+                              entry_page, entry_slot, 0, err);
+  }
+  return cudaSuccess;
 }
 
 int bc_merge_partials(int splits, int rows, int dim, const float* partial_ml,
