@@ -23,13 +23,15 @@
 // accumulator in TMEM (thread (w & 3)*32 + lane owns row = TMEM lane of that
 // index); they are merged in the epilogue. Warps 8 and 10 are the TMA
 // producers of K and of V (pages of the page table, then draft K/V): the copy
-// rate of paged boxes is bounded per issuing warp, so each ring has its own.
-// Warp 9 is the TMEM allocator and the single-thread MMA issuer. K and V tiles stream through separate rings: a K
+// rate of paged boxes is bounded per issuing warp. Warp 9 allocates TMEM and
+// issues the S = Q K^T MMAs from one thread, warp 11 the O += P V MMAs: a
+// tcgen05.mma costs its issuing thread about as long as a 128x64x16 MMA takes
+// to run, so one issuer per GEMM keeps the tensor pipe fed. K and V tiles stream through separate rings: a K
 // stage is released as soon as its S = Q K^T has been computed, a V stage once
 // its P V product is done, so the copies of later tiles are not held back by
-// the softmax of earlier ones (5 K stages, 8 V stages). S/P buffer g
-// belongs to group g, so both groups' softmax overlap each other and the MMAs
-// of their neighbouring tiles.
+// the softmax of earlier ones (5 K stages, 8 V stages). Three S/P buffers in
+// TMEM let S be computed two tiles ahead of PV, so a group's next S is ready
+// when its softmax ends.
 //
 // The running max is kept lazily: O and l are rescaled only when a row's max
 // grows by more than 2^8 (rare after the first tile), with probabilities up
@@ -50,7 +52,7 @@ constexpr int kTreeRows = 128;
 constexpr int kTreeTile = 64;        // keys per tile = 4 pages
 constexpr int kTreeKStages = 5;
 constexpr int kTreeVStages = 8;
-constexpr int kTreeThreads = 352;   // 8 softmax warps, K producer, MMA issuer, V producer
+constexpr int kTreeThreads = 384;   // 8 softmax warps, K producer, S issuer, V producer, PV issuer
 constexpr int kTreeMaxReq = 128;     // requests per CTA (rows per request >= 1)
 
 struct TreeParams {
@@ -79,13 +81,14 @@ struct TreeGeom {
   static constexpr int kKOff = 0;
   static constexpr int kVOff = kKOff + kKStages * kHalfTile;
   static constexpr int kBarOff = kVOff + kVStages * kHalfTile;
-  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 8 + 1 + 1;
+  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 3 + 3 + 2 + 2 + 1 + 1 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   // misc: tmem base (4) + nruns (4) + run tables 6 x kTreeMaxReq ints
   static constexpr int kRunOff = kMiscOff + 16;
   static constexpr int kWg1Off = kRunOff + 6 * kTreeMaxReq * 4;  // [128][2] second group's (m, l)
   static constexpr int kORowOff = kWg1Off + kTreeRows * 8;  // [128] output row of each tile row
-  static constexpr int kParOff = kORowOff + kTreeRows * 4;
+  static constexpr int kMlXOff = kORowOff + kTreeRows * 4;  // [2][128][2] each group's (m, l)
+  static constexpr int kParOff = kMlXOff + 2 * kTreeRows * 8;
   // Cluster merge (after the main loop, reusing the K/V rings):
   // kSlotRows received rows [source rank][row] at kKOff, then this CTA's own
   // 128 weighted rows (16-byte chunks XOR-swizzled by row) at kStageOff.
@@ -97,8 +100,10 @@ struct TreeGeom {
   // parent rows (anc_rows ints, 16-byte padded) then ancestor sets (32 B each)
   __host__ __device__ static size_t anc_offset(int anc_rows) { return size_t(kParOff) + ((size_t(anc_rows) * 4 + 15) & ~size_t(15)); }
   static size_t smem_bytes(int anc_rows) { return 1024 + anc_offset(anc_rows) + size_t(anc_rows) * 32; }
-  // TMEM columns: S/P of group g at 64 g, O of group g at 128 + 128 g, Q at 384.
-  static constexpr uint32_t kTmemO = 128, kTmemQ = 384;
+  // TMEM columns: three S/P buffers at 0, 64, 128 (tile i uses i % 3), O of
+  // group g at 192 + 128 g, Q at 448.
+  static constexpr int kSBufs = 3;
+  static constexpr uint32_t kTmemO = 192, kTmemQ = 448;
   static constexpr uint32_t kTmemCols = 512;
 };
 
@@ -122,11 +127,13 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   uint64_t* k_empty = k_full + G::kKStages;
   uint64_t* v_full = k_empty + G::kKStages;         // [kVStages]
   uint64_t* v_empty = v_full + G::kVStages;
-  uint64_t* s_full = v_empty + G::kVStages;         // [2]
-  uint64_t* p_full = s_full + 2;               // [2]
+  uint64_t* s_full = v_empty + G::kVStages;         // [3] per S/P buffer
+  uint64_t* p_full = s_full + G::kSBufs;       // [2] per softmax group
   uint64_t* pv_done = p_full + 2;              // [2]
-  uint64_t* mma_done = pv_done + 2;            // [1]
-  uint64_t* recv_done = mma_done + 1;          // [1] cluster merge: rows received
+  uint64_t* mma_done = pv_done + 2;            // [1] the S issuer's last MMA
+  uint64_t* s_free = mma_done + 1;             // [3] PV done reading S/P buffer b
+  uint64_t* pv_fin = s_free + G::kSBufs;       // [1] the PV issuer's last MMA
+  uint64_t* recv_done = pv_fin + 1;            // [1] cluster merge: rows received
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kMiscOff);
   int* nruns_s = reinterpret_cast<int*>(smem + G::kMiscOff + 4);
   int* run_first = reinterpret_cast<int*>(smem + G::kRunOff);  // first local request
@@ -224,8 +231,12 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < G::kSBufs; ++s) {
       mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 1);
+    }
+    mbar_init(pv_fin, 1);
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&p_full[s], 4);
       mbar_init(&pv_done[s], 1);
     }
@@ -337,7 +348,9 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
 
   if (warp == 8 || warp == 10) {
     // ------------------------------------------------------------ producers
+    // warp 8: K, warp 10: V
     const bool v_warp = warp == 10;
+    constexpr int part = 0, parts = 1, per_part = 4 * KB;  // boxes per tile
     if (ntiles > 0) {
       int run, t;
       start_cursor(v0, run, t);
@@ -378,11 +391,12 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           const bool ok = mbar_wait((is_v ? v_empty : k_empty) + st, ((i / nst) - 1) & 1);
           if (!__all_sync(0xffffffffu, ok)) return false;
         }
-        if (lane == 0) mbar_arrive_expect_tx(full, uint32_t(G::kHalfTile));
+        if (lane == 0) mbar_arrive_expect_tx(full, uint32_t(G::kHalfTile / parts));
         __syncwarp();
-        if (lane < 4 * KB) {
-          const int j = lane / KB;   // page of the tile
-          const int kb = lane % KB;  // 64-dim block
+        if (lane < per_part) {
+          const int box = part * per_part + lane;
+          const int j = box / KB;    // page of the tile
+          const int kb = box % KB;   // 64-dim block
           uint8_t* dst = smem + (is_v ? G::kVOff : G::kKOff) + st * G::kHalfTile +
                          kb * (kTreeTile * 128) + j * 2048;
           if (is_prefix) {
@@ -403,8 +417,9 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           next_ids = load_ids(i + 8);
         }
         const bool is_prefix = run < nruns;
-        // the page id of this lane's box (page lane / KB of the tile)
-        const int page_id = __shfl_sync(0xffffffffu, cur_ids, (i & 7) * 4 + min(lane / KB, 3));
+        // the page id of this lane's box
+        const int page_id = __shfl_sync(0xffffffffu, cur_ids,
+                                        (i & 7) * 4 + min((part * per_part + lane) / KB, 3));
         if (!v_warp && is_prefix && lane < 4 * KB && lane % KB == 0 &&
             (page_id >= p.physical_pages || page_id < -1))
           atomicOr(p.err, kErrPageRange);
@@ -420,17 +435,53 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       }
     }
   } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ S issuer
     if (ntiles > 0 && lane == 0) {
       bool ok = true;
-      auto issue_pv = [&](int i) {
+      for (int i = 0; i < ntiles && ok; ++i) {
+        const int kst = i % G::kKStages;
+        const int sb = i % G::kSBufs;
+        // S/P buffer sb was last used by tile i-3: its PV must have read P.
+        if (i >= G::kSBufs && !mbar_wait(&s_free[sb], ((i - G::kSBufs) / G::kSBufs) & 1)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&k_full[kst], (i / G::kKStages) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kbase = k_addr + kst * G::kHalfTile;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const int kb = ks >> 2, kin = ks & 3;
+          const uint64_t bdesc = umma_desc_sw128(kbase + kb * (kTreeTile * 128) + kin * 32, 16, 1024);
+          umma_f16_ts(tbase + uint32_t(sb) * 64, tbase + G::kTmemQ + ks * 8, bdesc, kIdescS,
+                      ks > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[kst]);  // K stage free once S is computed
+      }
+      if (!ok) atomicOr(p.err, kErrTimeout);
+      umma_commit(mma_done);
+      if (!mbar_wait(mma_done, 0)) atomicOr(p.err, kErrTimeout);
+    }
+  } else if (warp == 11) {
+    // ------------------------------------------------------------ PV issuer
+    if (ntiles > 0 && lane == 0) {
+      bool ok = true;
+      for (int i = 0; i < ntiles && ok; ++i) {
         const int vst = i % G::kVStages;
         const int buf = i & 1;
-        if (!mbar_wait(&p_full[buf], (i >> 1) & 1)) return false;
-        if (!mbar_wait(&v_full[vst], (i / G::kVStages) & 1)) return false;
+        const int sb = i % G::kSBufs;
+        if (!mbar_wait(&p_full[buf], (i >> 1) & 1) ||
+            !mbar_wait(&v_full[vst], (i / G::kVStages) & 1)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t vbase = v_addr + vst * G::kHalfTile;
-        const uint32_t tP = tbase + uint32_t(buf) * 64;           // P hi (+32: lo)
+        const uint32_t tP = tbase + uint32_t(sb) * 64;                // P hi (+32: lo)
         const uint32_t tO = tbase + G::kTmemO + uint32_t(buf) * 128;  // group buf's O
 #pragma unroll
         for (int kk = 0; kk < kTreeTile / 16; ++kk) {
@@ -443,31 +494,11 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         }
         umma_commit(&pv_done[buf]);
         umma_commit(&v_empty[vst]);
-        return true;
-      };
-      for (int i = 0; i < ntiles && ok; ++i) {
-        const int kst = i % G::kKStages;
-        if (!mbar_wait(&k_full[kst], (i / G::kKStages) & 1)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t kbase = k_addr + kst * G::kHalfTile;
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const int kb = ks >> 2, kin = ks & 3;
-          const uint64_t bdesc = umma_desc_sw128(kbase + kb * (kTreeTile * 128) + kin * 32, 16, 1024);
-          umma_f16_ts(tbase + uint32_t(i & 1) * 64, tbase + G::kTmemQ + ks * 8, bdesc, kIdescS,
-                      ks > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[i & 1]);
-        umma_commit(&k_empty[kst]);  // K stage free once S is computed
-        if (i > 0) ok = issue_pv(i - 1);
+        umma_commit(&s_free[sb]);
       }
-      if (ok) ok = issue_pv(ntiles - 1);
       if (!ok) atomicOr(p.err, kErrTimeout);
-      umma_commit(mma_done);
-      if (!mbar_wait(mma_done, 0)) atomicOr(p.err, kErrTimeout);
+      umma_commit(pv_fin);
+      if (!mbar_wait(pv_fin, 0)) atomicOr(p.err, kErrTimeout);
     }
   }
 
@@ -486,8 +517,9 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     start_cursor(v0 + wg, run, t);
     const uint32_t* my_anc = anc + (size_t(max(my_req, 0)) * p.nodes + my_node) * 8;
     for (int i = wg; i < ntiles; i += 2) {
-      const int buf = i & 1;
-      if (!mbar_wait(&s_full[buf], (i >> 1) & 1)) {
+      const int buf = i & 1;            // this group's P barrier and O accumulator
+      const int sb = i % G::kSBufs;     // the S/P buffer of tile i
+      if (!mbar_wait(&s_full[sb], (i / G::kSBufs) & 1)) {
         softmax_ok = false;
         break;
       }
@@ -496,8 +528,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       {
         uint32_t (&s0)[32] = *reinterpret_cast<uint32_t (*)[32]>(&s[0]);
         uint32_t (&s1)[32] = *reinterpret_cast<uint32_t (*)[32]>(&s[32]);
-        tmem_ld32(tbase + lane_addr + buf * 64, s0);
-        tmem_ld32(tbase + lane_addr + buf * 64 + 32, s1);
+        tmem_ld32(tbase + lane_addr + sb * 64, s0);
+        tmem_ld32(tbase + lane_addr + sb * 64 + 32, s1);
         tmem_ld_wait();
       }
       // Masking: prefix keys of this row's run below the run length; draft
@@ -553,12 +585,6 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         l_sum *= alpha;
       }
       const float mb = m_ref == kNegInf ? 0.f : m_ref;
-      // This group's O is free for the rescale once PV of tile i-2 is done
-      // (already implied by S(i) being complete: the MMAs run in issue order).
-      if (i >= 2 && !mbar_wait(&pv_done[buf], ((i - 2) >> 1) & 1)) {
-        softmax_ok = false;
-        break;
-      }
       // P over S's own TMEM columns: hi at +0, lo at +32 (FP16 pairs), in
       // two halves of 32 keys to bound the live registers.
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
@@ -585,8 +611,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
             ph[e / 2] = pack_half2(p0, p1);
           }
         }
-        tmem_st16(tbase + lane_addr + uint32_t(buf) * 64 + half * 16, ph);
-        if (PREC) tmem_st16(tbase + lane_addr + uint32_t(buf) * 64 + 32 + half * 16, pl);
+        tmem_st16(tbase + lane_addr + uint32_t(sb) * 64 + half * 16, ph);
+        if (PREC) tmem_st16(tbase + lane_addr + uint32_t(sb) * 64 + 32 + half * 16, pl);
       }
       l_sum += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // Keys past a prefix run's end may hold anything: zero their V rows so
@@ -608,9 +634,15 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         }
         fence_proxy_async_smem();
       }
-      // O rescale (whole warp when any of its rows needs it). This group's
-      // previous PV (tile i-2) is complete: it was waited for above.
+      // O rescale (whole warp when any of its rows needs it), once this
+      // group's previous PV (tile i-2) has completed. (P(i) itself needs no
+      // wait: S(i) completing means every earlier MMA, among them the PV
+      // that last read this S/P buffer, has completed.)
       if (__any_sync(0xffffffffu, rescale)) {
+        if (i >= 2 && !mbar_wait(&pv_done[buf], ((i - 2) >> 1) & 1)) {
+          softmax_ok = false;
+          break;
+        }
         tc_fence_after();
         const float f = rescale ? alpha : 1.f;
 #pragma unroll
@@ -660,11 +692,17 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base) = make_float4(a, b, c, d);
     }
   };
-  // Group 1 hands its (m, l) to group 0 through shared memory; group 0 then
-  // publishes the CTA's (m, l) per row in the same place for the cluster.
-  float* wg1_ml = reinterpret_cast<float*>(smem + G::kWg1Off);
+  // The two groups exchange their per-row (m, l) through shared memory, so
+  // every softmax thread knows its row's merged state; warps w and w+4 share
+  // TMEM lanes (rows) and each moves one half of the row's D columns.
+  float* ml_x = reinterpret_cast<float*>(smem + G::kMlXOff);  // [group][row][m, l]
+  float* cl_ml = reinterpret_cast<float*>(smem + G::kWg1Off);  // [row][m, l], read by peers
   int* orow = reinterpret_cast<int*>(smem + G::kORowOff);
+  constexpr int kHalfD = D / 2;
+  const int col0 = wg * kHalfD;  // this thread's columns of O
   bool have = false;
+  float w0 = 0.f, w1 = 0.f, mm = kNegInf;
+  float f[kHalfD];  // this thread's part of the row: w0 * O0 + w1 * O1
   if (warp < 8) {
     have = ntiles > wg && softmax_ok;
     const int last = have ? wg + 2 * ((ntiles - 1 - wg) / 2) : 0;
@@ -672,32 +710,44 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       have = false;
       if (lane == 0) atomicOr(p.err, kErrTimeout);
     }
-    if (wg == 1) {
-      wg1_ml[r * 2 + 0] = have ? m_ref : kNegInf;
-      wg1_ml[r * 2 + 1] = have ? l_sum : 0.f;
-    }
+    ml_x[(wg * kTreeRows + r) * 2 + 0] = have ? m_ref : kNegInf;
+    ml_x[(wg * kTreeRows + r) * 2 + 1] = have ? l_sum : 0.f;
     named_barrier_sync(2, 256);
-  }
-  // Weights of the two groups' accumulators: final O = w0 * O0 + w1 * O1.
-  float w0 = 0.f, w1 = 0.f, mm = kNegInf;
-  bool use0 = false, use1 = false;
-  if (warp < 4) {
-    const float m1 = wg1_ml[r * 2 + 0], l1 = wg1_ml[r * 2 + 1];
-    const float m0 = have ? m_ref : kNegInf, l0 = have ? l_sum : 0.f;
+    const float m0 = ml_x[r * 2 + 0], l0 = ml_x[r * 2 + 1];
+    const float m1 = ml_x[(kTreeRows + r) * 2 + 0], l1 = ml_x[(kTreeRows + r) * 2 + 1];
     mm = fmaxf(m0, m1);
     // A group contributes only if its max is finite (it saw a valid key).
-    use0 = m0 != kNegInf;
-    use1 = m1 != kNegInf;
+    const bool use0 = m0 != kNegInf, use1 = m1 != kNegInf;
     w0 = use0 ? fast_exp2(m0 - mm) : 0.f;
     w1 = use1 ? fast_exp2(m1 - mm) : 0.f;
     const float lsum = w0 * l0 + w1 * l1;
     if (to_cluster) {
-      wg1_ml[r * 2 + 0] = mm;
-      wg1_ml[r * 2 + 1] = lsum;
+      if (wg == 0) {
+        cl_ml[r * 2 + 0] = mm;
+        cl_ml[r * 2 + 1] = lsum;
+      }
     } else {
       const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
       w0 *= inv;
       w1 *= inv;
+    }
+    // O from TMEM (before the cluster barrier: the loads overlap its wait).
+    // The reads are warp-collective: they depend only on whether the group
+    // processed any tile at all (uniform across the warp).
+    tc_fence_after();
+    const bool read0 = ntiles > 0, read1 = ntiles > 1;
+#pragma unroll
+    for (int h = 0; h < kHalfD / 32; ++h) {
+      uint32_t o[32], o1[32];
+      if (read0) tmem_ld32(tbase + lane_addr + G::kTmemO + col0 + 32 * h, o);
+      if (read1) tmem_ld32(tbase + lane_addr + G::kTmemO + 128 + col0 + 32 * h, o1);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float a = (read0 && use0) ? w0 * __uint_as_float(o[e]) : 0.f;
+        const float b = (read1 && use1) ? w1 * __uint_as_float(o1[e]) : 0.f;
+        f[32 * h + e] = a + b;
+      }
     }
   }
   // Rows of this tile owned by this CTA in the cluster merge.
@@ -706,64 +756,41 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     mbar_arrive_expect_tx(recv_done, uint32_t((csize - 1) * own_rows * G::kRowBytes));
   if (to_cluster) {
     cluster_sync_all();  // every CTA's (m, l) is final and its rings are idle
-    if (warp < 4 && r < valid_rows) {
-      const uint32_t ml_addr = smem_u32(wg1_ml + r * 2);
-      float2 mlc[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        if (c < csize) mlc[c] = ld_cluster_f32x2(map_to_rank(ml_addr, uint32_t(c)));
-      float M = kNegInf;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        if (c < csize) M = fmaxf(M, mlc[c].x);
-      float L = 0.f;
-      if (M != kNegInf) {
+    if (warp < 8) {
+      float share = 0.f;
+      if (r < valid_rows) {
+        const uint32_t ml_addr = smem_u32(cl_ml + r * 2);
+        float2 mlc[8];
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          if (c < csize && mlc[c].x != kNegInf) L += fast_exp2(mlc[c].x - M) * mlc[c].y;
-      }
-      // This CTA's share of the row: exp2(mm - M) / L (0 for a CTA without keys).
-      const float share = (mm != kNegInf && L > 0.f) ? fast_exp2(mm - M) / L : 0.f;
-      w0 *= share;
-      w1 *= share;
-    }
-  }
-  if (warp < 4) {
-    tc_fence_after();
-    // The TMEM reads are warp-collective: they depend only on whether the
-    // group processed any tile at all (uniform across the warp).
-    const bool read0 = ntiles > 0, read1 = ntiles > 1;
-    uint8_t* srow = smem + G::kStageOff + r * G::kRowBytes;
-    const size_t obase = r < valid_rows ? out_ptr(r) : 0;
-    if (to_cluster) orow[r] = int(obase / D);
-#pragma unroll 1
-    for (int c = 0; c < D; c += 32) {
-      uint32_t o[32], o1[32];
-      if (read0) tmem_ld32(tbase + lane_addr + G::kTmemO + c, o);
-      if (read1) tmem_ld32(tbase + lane_addr + G::kTmemO + 128 + c, o1);
-      tmem_ld_wait();
-      float f[32];
+          if (c < csize) mlc[c] = ld_cluster_f32x2(map_to_rank(ml_addr, uint32_t(c)));
+        float M = kNegInf;
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float a = (read0 && use0) ? w0 * __uint_as_float(o[e]) : 0.f;
-        const float b = (read1 && use1) ? w1 * __uint_as_float(o1[e]) : 0.f;
-        f[e] = a + b;
-      }
-      if (r < valid_rows) {
-        if (to_cluster) {
+        for (int c = 0; c < 8; ++c)
+          if (c < csize) M = fmaxf(M, mlc[c].x);
+        float L = 0.f;
+        if (M != kNegInf) {
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            const int chunk = (c + e) >> 2;
-            *reinterpret_cast<float4*>(srow + ((chunk ^ (r & 7)) << 4)) =
-                make_float4(f[e], f[e + 1], f[e + 2], f[e + 3]);
-          }
-        } else {
+          for (int c = 0; c < 8; ++c)
+            if (c < csize && mlc[c].x != kNegInf) L += fast_exp2(mlc[c].x - M) * mlc[c].y;
+        }
+        // This CTA's share of the row: exp2(mm - M) / L (0 for a CTA without keys).
+        share = (mm != kNegInf && L > 0.f) ? fast_exp2(mm - M) / L : 0.f;
+        if (wg == 0) orow[r] = int(out_ptr(r) / D);
+        uint8_t* srow = smem + G::kStageOff + r * G::kRowBytes;
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) store_out4(obase + c + e, f[e], f[e + 1], f[e + 2], f[e + 3]);
+        for (int e = 0; e < kHalfD; e += 4) {
+          const int chunk = (col0 + e) >> 2;
+          *reinterpret_cast<float4*>(srow + ((chunk ^ (r & 7)) << 4)) =
+              make_float4(f[e] * share, f[e + 1] * share, f[e + 2] * share, f[e + 3] * share);
         }
       }
+      fence_proxy_async_smem();  // staged rows -> the bulk copies
     }
-    if (to_cluster) fence_proxy_async_smem();  // staged rows -> the bulk copies
+  } else if (warp < 8 && r < valid_rows) {
+    const size_t base = out_ptr(r) + col0;
+#pragma unroll
+    for (int e = 0; e < kHalfD; e += 4) store_out4(base + e, f[e], f[e + 1], f[e + 2], f[e + 3]);
   }
   tc_fence_before();
   __syncthreads();
@@ -800,16 +827,25 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         const int rl = task / (D / 4), chunk = task % (D / 4);
         const int row = row0 + rl;
         const int off = ((chunk ^ (row & 7)) << 4);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = 0; c < csize; ++c) {
-          const uint8_t* src = c == int(rank)
-                                   ? smem + G::kStageOff + row * G::kRowBytes
-                                   : smem + G::kKOff + (c * rpk + rl) * G::kRowBytes;
-          const float4 v = *reinterpret_cast<const float4*>(src + off);
-          acc.x += v.x;
-          acc.y += v.y;
-          acc.z += v.z;
-          acc.w += v.w;
+        float4 v[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          if (c < csize) {
+            const uint8_t* src = c == int(rank)
+                                     ? smem + G::kStageOff + row * G::kRowBytes
+                                     : smem + G::kKOff + (c * rpk + rl) * G::kRowBytes;
+            v[c] = *reinterpret_cast<const float4*>(src + off);
+          }
+        }
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);  // rank order: deterministic
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          if (c < csize) {
+            acc.x += v[c].x;
+            acc.y += v[c].y;
+            acc.z += v[c].z;
+            acc.w += v[c].w;
+          }
         }
         store_out4(size_t(orow[row]) * D + chunk * 4, acc.x, acc.y, acc.z, acc.w);
       }
