@@ -531,6 +531,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         tmem_ld32(tbase + lane_addr + sb * 64, s0);
         tmem_ld32(tbase + lane_addr + sb * 64 + 32, s1);
         tmem_ld_wait();
+        tmem_bind32(s0);
+        tmem_bind32(s1);
       }
       // Masking: prefix keys of this row's run below the run length; draft
       // slots of this row's request that are ancestors-or-self of its node.
@@ -650,6 +652,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           uint32_t o[32];
           tmem_ld32(tbase + lane_addr + o_col + c, o);
           tmem_ld_wait();
+          tmem_bind32(o);
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
           tmem_st32(tbase + lane_addr + o_col + c, o);
@@ -742,6 +745,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       if (read0) tmem_ld32(tbase + lane_addr + G::kTmemO + col0 + 32 * h, o);
       if (read1) tmem_ld32(tbase + lane_addr + G::kTmemO + 128 + col0 + 32 * h, o1);
       tmem_ld_wait();
+      if (read0) tmem_bind32(o);
+      if (read1) tmem_bind32(o1);
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
         const float a = (read0 && use0) ? w0 * __uint_as_float(o[e]) : 0.f;
