@@ -150,13 +150,6 @@ def to_dev(torch, a, device):
     return torch.from_numpy(a.copy()).to(device)
 
 
-def pinned(torch, a):
-    a = np.ascontiguousarray(a)
-    t = (torch.from_numpy(a.view(np.int16).copy()).view(torch.float16) if a.dtype == np.uint16
-         else torch.from_numpy(a.copy()))
-    return t.pin_memory()
-
-
 def half_bits(torch, t):
     return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
 
