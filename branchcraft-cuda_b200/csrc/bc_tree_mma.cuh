@@ -161,13 +161,46 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   const int b0 = blk * p.req_per_block;
   const int nreq = min(p.req_per_block, p.batch - b0);
   const int npad = (p.nodes + 15) & ~15;              // draft slots per request
+  // Set-up that reads no input runs before the wait for the preceding kernel
+  // (a programmatic dependent launch may start while that kernel finishes):
+  // barriers, the TMEM allocation, the tensor-map prefetch.
+  if (tid == 0) {
+    for (int s = 0; s < G::kKStages; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < G::kVStages; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int s = 0; s < G::kSBufs; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 1);
+    }
+    mbar_init(pv_fin, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&p_full[s], 4);
+      mbar_init(&pv_done[s], 1);
+    }
+    mbar_init(mma_done, 1);
+    mbar_init(recv_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, G::kTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  if ((warp == 8 || warp == 10) && lane == 0) {
+    prefetch_tmap(warp == 8 ? &kmap : &vmap);
+    prefetch_tmap(warp == 8 ? &dkmap : &dvmap);
+  }
   grid_dependency_wait();  // inputs written by the preceding kernel are visible
 
   // ---- prologue. Every global load of the prologue (lengths, parent rows,
   // page-row comparisons, query rows, the producer's speculative page ids) is
   // issued before any of their results is used, so the CTA pays one memory
-  // round trip before its first K/V copy; barrier set-up and the TMEM
-  // allocation overlap it.
+  // round trip before its first K/V copy.
   const int cap = p.max_pages * kPageSize;
   const int ndraft_tiles = (nreq * npad + kTreeTile - 1) / kTreeTile;
   const int npar = nreq * p.nodes;              // <= 256: R * nodes (host)
@@ -221,33 +254,6 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     };
     cur_ids = spec_id(lane >> 2);
     next_ids = spec_id(8 + (lane >> 2));
-  }
-  if (tid == 0) {
-    for (int s = 0; s < G::kKStages; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-    }
-    for (int s = 0; s < G::kVStages; ++s) {
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
-    }
-    for (int s = 0; s < G::kSBufs; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_free[s], 1);
-    }
-    mbar_init(pv_fin, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&p_full[s], 4);
-      mbar_init(&pv_done[s], 1);
-    }
-    mbar_init(mma_done, 1);
-    mbar_init(recv_done, 1);
-    fence_mbar_init();
-  }
-  if (warp == 9) {
-    tmem_alloc(tmem_slot, G::kTmemCols);
-    tmem_relinquish();
-    tc_fence_before();
   }
   for (int i = tid; i < nreq; i += kTreeThreads) mismatch[i] = 0x7fffffff;
   __syncthreads();
@@ -354,7 +360,6 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     if (ntiles > 0) {
       int run, t;
       start_cursor(v0, run, t);
-      if (lane == 0) prefetch_tmap(v_warp ? &vmap : &kmap);
       // Lane l holds the page id of page (l & 3) of tile (batch*8 + l/4); the
       // next batch is loaded while this one is issued. The prologue's
       // speculative ids stand when the block is one run of request b0.
