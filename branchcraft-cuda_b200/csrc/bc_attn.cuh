@@ -110,6 +110,18 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int kvh = bk / p.batch;
   const int split = blockIdx.z;
 
+  // Barriers need no input: set them up before waiting for the preceding
+  // kernel (a programmatic dependent launch may start while it finishes).
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  grid_dependency_wait();
+
   int len = p.lengths[b];
   const int cap = p.max_pages * kPageSize;
   if (len < 0 || len > cap) {
@@ -123,14 +135,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int vend = min(nv, vbeg + per);
   const int nstages = (vend - vbeg + kPagesPerStage - 1) / kPagesPerStage;
 
-  if (threadIdx.x == 0) {
-#pragma unroll
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
-    }
-    fence_mbar_init();
-  }
   __syncthreads();
 
   if (warp == kConsumerWarps) {
@@ -359,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   // ---- merge the page groups of this CTA, then finish by split mode
+  grid_launch_dependents();  // the merge kernel may be scheduled (it waits for this grid)
   float* mo = reinterpret_cast<float*>(smem);
   float* mml = mo + kConsumerWarps * 8 * OS;
   float* fo = mml + kConsumerWarps * 8 * 2;  // [ROWS][OS] CTA result
@@ -487,6 +492,7 @@ __global__ void __launch_bounds__(128)
   constexpr int R = D / 32;
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  grid_dependency_wait();  // the partials of the preceding kernel are visible
   if (row >= rows) return;
   float mmax = -INFINITY;
   for (int s = 0; s < splits; ++s) mmax = fmaxf(mmax, pml[(size_t(s) * rows + row) * 2]);

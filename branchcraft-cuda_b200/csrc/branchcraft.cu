@@ -126,6 +126,23 @@ bool encode_draft_map(CUtensorMap* map, const void* base, int dim, int heads, in
 }
 
 // ---------------------------------------------------------------- launches
+// FP32 merge of split partials, a programmatic dependent of the kernel that
+// wrote them.
+cudaError_t launch_merge(int dim, int rows, int splits, const float* pml, const float* pa,
+                         float* out, cudaStream_t stream) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned((rows + 3) / 4), 1, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return dim == 64 ? cudaLaunchKernelEx(&cfg, merge_kernel<64>, rows, splits, pml, pa, out)
+                   : cudaLaunchKernelEx(&cfg, merge_kernel<128>, rows, splits, pml, pa, out);
+}
+
 template <int D, int RT, bool OUT_HALF>
 cudaError_t launch_attn_t(const AttnParams& p, const CUtensorMap* maps, int items, int cluster,
                           cudaStream_t stream) {
@@ -145,14 +162,19 @@ cudaError_t launch_attn_t(const AttnParams& p, const CUtensorMap* maps, int item
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  // Programmatic dependent launch: scheduled while the preceding kernel
+  // finishes, waiting for it before the first input read.
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (cluster > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = unsigned(cluster);
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = unsigned(cluster);
+    cfg.numAttrs = 2;
   }
   return cudaLaunchKernelEx(&cfg, kern, p, maps[0], maps[1]);
 }
@@ -256,13 +278,8 @@ cudaError_t paged_decode_core(const bc_shape* s, const void* q, const void* k, c
   cudaError_t e = launch_attn(s->dim, rt, out_half, p, maps, int(items), cluster, stream);
   if (e != cudaSuccess || mode != kSplitGlobal || emit_partial) return e;
   const int rows = s->batch * s->query_heads;
-  if (s->dim == 64)
-    merge_kernel<64><<<(rows + 3) / 4, 128, 0, stream>>>(rows, splits, partial_ml, partial_a,
-                                                         static_cast<float*>(out));
-  else
-    merge_kernel<128><<<(rows + 3) / 4, 128, 0, stream>>>(rows, splits, partial_ml, partial_a,
-                                                          static_cast<float*>(out));
-  return cudaGetLastError();
+  return launch_merge(s->dim, rows, splits, partial_ml, partial_a, static_cast<float*>(out),
+                      stream);
 }
 
 int pick_mode(int splits) { return splits <= 1 ? kSplitNone : splits <= 8 ? kSplitCluster : kSplitGlobal; }
@@ -623,12 +640,8 @@ int bc_merge_partials(int splits, int rows, int dim, const float* partial_ml,
                       const float* partial_a, float* out, void* stream) {
   if (splits < 1 || rows < 1 || (dim != 64 && dim != 128) || !partial_ml || !partial_a || !out)
     return cudaErrorInvalidValue;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (dim == 64)
-    merge_kernel<64><<<(rows + 3) / 4, 128, 0, st>>>(rows, splits, partial_ml, partial_a, out);
-  else
-    merge_kernel<128><<<(rows + 3) / 4, 128, 0, st>>>(rows, splits, partial_ml, partial_a, out);
-  return cudaGetLastError();
+  return launch_merge(dim, rows, splits, partial_ml, partial_a, out,
+                      static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------
