@@ -463,11 +463,13 @@ int bc_auto_splits(const bc_shape* s, int max_length, int sm_count_arg) {
   int rt = 1, chunks = 1;
   row_tiling(g < 1 ? 1 : g, &rt, &chunks);
   const long long base = (long long)(s->batch > 0 ? s->batch : 1) * groups * chunks;
-  const long long wanted = (2LL * (sm_count_arg > 0 ? sm_count_arg : 148) + base - 1) / base;
-  int splits = 1;
-  while (splits < wanted && splits < BC_MAX_SPLITS) splits *= 2;
-  while (splits > 1 && max_length / splits < 256) splits /= 2;
-  return splits;
+  // As many splits as make one wave of CTAs (two resident per SM): a second,
+  // partial wave costs more than the longer key range of fewer splits. Any
+  // count works (the merge takes 1..64); each split keeps >= 256 keys.
+  const long long wave = 2LL * (sm_count_arg > 0 ? sm_count_arg : 148);
+  long long splits = std::max(1LL, std::min<long long>(BC_MAX_SPLITS, wave / base));
+  splits = std::min<long long>(splits, std::max(1, max_length / 256));
+  return int(splits);
 }
 
 int bc_paged_decode(const bc_shape* s, const void* q, const void* k, const void* v,

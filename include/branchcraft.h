@@ -64,7 +64,9 @@ int bc_decode(const bc_shape* shape, const void* q, const void* k, const void* v
 
 /* Split-count heuristic for bc_decode. Replaces branchcraft::auto_splits
  * (reference include/branchcraft.hpp:41, src/paged_gqa.cu:134-142), retuned for
- * this kernel's CTA shape (one CTA per request and KV head) and splits <= 64. */
+ * this kernel's CTA shape (one CTA per request and KV head): the largest count,
+ * at most 64 and leaving each split >= 256 keys, whose CTAs fit one wave of two
+ * per SM. */
 int bc_auto_splits(const bc_shape* shape, int max_length, int sm_count);
 
 /* Paged decode with the split count chosen by the library (splits <= 0) or
