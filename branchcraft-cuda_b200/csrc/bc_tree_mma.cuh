@@ -18,20 +18,23 @@
 // A operands read from tensor memory, so shared memory carries only the K/V
 // tiles: per tile the tensor cores read K once and V once per P part.
 //
-// Warp roles (352 threads): two softmax warpgroups (warps 0-3 and 4-7) take
+// Warp roles (512 threads): two softmax warpgroups (warps 0-3 and 4-7) take
 // alternate key tiles, each with its own online-softmax state and its own O
 // accumulator in TMEM (thread (w & 3)*32 + lane owns row = TMEM lane of that
-// index); they are merged in the epilogue. Warps 8 and 10 are the TMA
-// producers of K and of V (pages of the page table, then draft K/V): the copy
-// rate of paged boxes is bounded per issuing warp. Warp 9 allocates TMEM and
-// issues the S = Q K^T MMAs from one thread, warp 11 the O += P V MMAs: a
-// tcgen05.mma costs its issuing thread about as long as a 128x64x16 MMA takes
-// to run, so one issuer per GEMM keeps the tensor pipe fed. K and V tiles stream through separate rings: a K
-// stage is released as soon as its S = Q K^T has been computed, a V stage once
-// its P V product is done, so the copies of later tiles are not held back by
-// the softmax of earlier ones (5 K stages, 8 V stages). Three S/P buffers in
-// TMEM let S be computed two tiles ahead of PV, so a group's next S is ready
-// when its softmax ends.
+// index); they are merged in the epilogue. Warps 8 and 12 are the TMA
+// producers of K, warps 10 and 14 those of V (pages of the page table, then
+// draft K/V), each of a pair taking alternate tiles: the copy rate of paged
+// boxes is bounded per issuing warp. Warp 9 allocates TMEM and issues the
+// S = Q K^T MMAs from one thread, warp 11 the O += P V MMAs: a tcgen05.mma
+// costs its issuing thread about as long as a 128x64x16 MMA takes to run, so
+// one issuer per GEMM keeps the tensor pipe fed. Warps 13 and 15 only take
+// part in the epilogue. After the prologue the softmax warpgroups take
+// registers from the other two (setmaxnreg). K and V tiles stream through
+// separate rings: a K stage is released as soon as its S = Q K^T has been
+// computed, a V stage once its P V product is done, so the copies of later
+// tiles are not held back by the softmax of earlier ones (5 K stages, 8 V
+// stages). Three S/P buffers in TMEM let S be computed two tiles ahead of PV,
+// so a group's next S is ready when its softmax ends.
 //
 // The running max is kept lazily: O and l are rescaled only when a row's max
 // grows by more than 2^8 (rare after the first tile), with probabilities up
@@ -52,7 +55,17 @@ constexpr int kTreeRows = 128;
 constexpr int kTreeTile = 64;        // keys per tile = 4 pages
 constexpr int kTreeKStages = 5;
 constexpr int kTreeVStages = 8;
-constexpr int kTreeThreads = 384;   // 8 softmax warps, K producer, S issuer, V producer, PV issuer
+constexpr int kTreeThreads = 512;   // 8 softmax warps, 4 TMA producers, S issuer, PV issuer, 2 idle
+// Registers: launched at 128 per thread (65,536 / 512); after the prologue
+// the softmax warpgroups grow to 160 and the other two shrink to 96
+// (2 x 128 x 160 + 2 x 128 x 96 = 65,536: the whole launch budget; both
+// paths compile without spills at these budgets).
+constexpr int kTreeLaunchRegs = 128;
+constexpr int kTreeSoftmaxRegs = 160;
+constexpr int kTreeOtherRegs = 96;
+static_assert(2 * 128 * kTreeSoftmaxRegs + 2 * 128 * kTreeOtherRegs ==
+                  kTreeThreads * kTreeLaunchRegs,
+              "the register split must use exactly the launch budget");
 constexpr int kTreeMaxReq = 128;     // requests per CTA (rows per request >= 1)
 
 struct TreeParams {
@@ -195,6 +208,11 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     prefetch_tmap(warp == 8 ? &kmap : &vmap);
     prefetch_tmap(warp == 8 ? &dkmap : &dvmap);
   }
+  // TMA producers: warps 8 and 12 copy K, 10 and 14 copy V; warps 8 / 10
+  // take the even tiles, 12 / 14 the odd ones (the issue rate of paged boxes
+  // is bounded per issuing warp).
+  const bool producer = warp == 8 || warp == 10 || warp == 12 || warp == 14;
+  const int psub = warp >= 12 ? 1 : 0;  // tile parity of a producer warp
   grid_dependency_wait();  // inputs written by the preceding kernel are visible
 
   // ---- prologue. Every global load of the prologue (lengths, parent rows,
@@ -241,12 +259,12 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // table; the producer checks the guess after phase 2.
   const int spec_t0 = (cap + kTreeTile - 1) / kTreeTile;
   int cur_ids = -1, next_ids = -1;
-  if (warp == 8 || warp == 10) {
+  if (producer) {
     const int tot = spec_t0 + ndraft_tiles;
     const int per0 = (tot + p.splits - 1) / p.splits;
     const int spec_v0 = min(tot, split * per0);
-    auto spec_id = [&](int i) -> int {
-      const int v = spec_v0 + i;
+    auto spec_id = [&](int i) -> int {  // i: this warp's i-th tile
+      const int v = spec_v0 + psub + 2 * i;
       if (v >= spec_t0) return -1;
       const int pg = v * 4 + (lane & 3);
       if (pg >= p.max_pages) return -1;
@@ -352,19 +370,97 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   const uint32_t k_addr = smem_u32(smem + G::kKOff);
   const uint32_t v_addr = smem_u32(smem + G::kVOff);
 
-  if (warp == 8 || warp == 10) {
+  const bool to_cluster = p.splits > 1;
+  const int csize = p.splits;
+  const uint32_t rank = to_cluster ? cluster_ctarank() : 0u;
+  const int rpk = (kTreeRows + csize - 1) / csize;  // rows owned by each CTA of the cluster
+  const int valid_rows = min(kTreeRows, nreq * p.rows_req - trow * kTreeRows);
+  auto out_ptr = [&](int row) -> size_t {
+    const int br = trow * kTreeRows + row;
+    const int rq = br / p.rows_req, node = (br % p.rows_req) / p.group, hh = br % p.group;
+    return ((size_t(b0 + rq) * p.nodes + node) * p.hq + size_t(kvh) * p.group + hh) * D;
+  };
+  auto store_out4 = [&](size_t base, float a, float b, float c, float d) {
+    if constexpr (OUT_HALF) {
+      uint2 v;
+      v.x = pack_half2(a, b);
+      v.y = pack_half2(c, d);
+      *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.out) + base) = v;
+    } else {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base) = make_float4(a, b, c, d);
+    }
+  };
+  int* orow = reinterpret_cast<int*>(smem + G::kORowOff);
+  // Rows of this tile owned by this CTA in the cluster merge.
+  const int own_rows = to_cluster ? max(0, min(rpk, valid_rows - int(rank) * rpk)) : 0;
+  // The cluster merge's last step, shared by all 512 threads: wait for the
+  // peers' rows, sum each owned row's slots in rank order and store it.
+  auto merge_owned_rows = [&]() {
+    bool got = true;
+    if (own_rows > 0) got = mbar_wait(recv_done, 0);
+    // Every row this CTA owns has arrived, so every copy into it is done:
+    // announce that now, and wait for the peers only before leaving.
+    cluster_arrive_relaxed();
+    if (!got) {
+      if (tid == 0) atomicOr(p.err, kErrTimeout);
+    } else {
+      const int row0 = int(rank) * rpk;
+      for (int task = tid; task < own_rows * (D / 4); task += kTreeThreads) {
+        const int rl = task / (D / 4), chunk = task % (D / 4);
+        const int row = row0 + rl;
+        const int off = ((chunk ^ (row & 7)) << 4);
+        float4 v[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          if (c < csize) {
+            const uint8_t* src = c == int(rank)
+                                     ? smem + G::kStageOff + row * G::kRowBytes
+                                     : smem + G::kKOff + (c * rpk + rl) * G::kRowBytes;
+            v[c] = *reinterpret_cast<const float4*>(src + off);
+          }
+        }
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);  // rank order: deterministic
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          if (c < csize) {
+            acc.x += v[c].x;
+            acc.y += v[c].y;
+            acc.z += v[c].z;
+            acc.w += v[c].w;
+          }
+        }
+        store_out4(size_t(orow[row]) * D + chunk * 4, acc.x, acc.y, acc.z, acc.w);
+      }
+    }
+    cluster_wait();  // no CTA leaves while its staged rows may still be read
+  };
+
+  // Warps 8-15 (producers, MMA issuers, two idle warps) give up registers to
+  // the softmax warpgroups. The two paths never rejoin (this one returns after
+  // its share of the epilogue), so each is compiled to its own budget.
+  if (warp >= 8) {
+  regs_decrease<kTreeOtherRegs>();
+  if (producer) {
     // ------------------------------------------------------------ producers
-    // warp 8: K, warp 10: V
-    const bool v_warp = warp == 10;
-    constexpr int part = 0, parts = 1, per_part = 4 * KB;  // boxes per tile
-    if (ntiles > 0) {
+    // warps 8 / 12: K, warps 10 / 14: V; tiles of parity psub
+    const bool v_warp = warp == 10 || warp == 14;
+    constexpr int per_part = 4 * KB;  // boxes per tile
+    if (ntiles > psub) {
       int run, t;
-      start_cursor(v0, run, t);
-      // Lane l holds the page id of page (l & 3) of tile (batch*8 + l/4); the
+      start_cursor(v0 + psub, run, t);
+      auto step = [&]() {  // the cursor to the next tile
+        ++t;
+        while (run < nruns && t >= run_tiles[run]) {  // empty runs have no tiles
+          t -= run_tiles[run];
+          ++run;
+        }
+      };
+      // Lane l holds the page id of page (l & 3) of this warp's tile
+      // (batch*8 + l/4), i.e. tile psub + 2 (batch*8 + l/4) of the CTA; the
       // next batch is loaded while this one is issued. The prologue's
       // speculative ids stand when the block is one run of request b0.
       auto load_ids = [&](int batch_first) -> int {
-        const int i = batch_first + (lane >> 2);
+        const int i = psub + 2 * (batch_first + (lane >> 2));
         if (i >= ntiles) return -1;
         int rr, tt;
         start_cursor(v0 + i, rr, tt);
@@ -377,7 +473,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         // The speculation held (one run, as many prefix tiles as the table
         // width, hence the same key range): mask the pages past the length.
         auto mask = [&](int id, int first) -> int {
-          const int pg = (v0 + first + (lane >> 2)) * 4 + (lane & 3);
+          const int pg = (v0 + psub + 2 * (first + (lane >> 2))) * 4 + (lane & 3);
           return pg * kPageSize >= run_len[0] ? -1 : id;
         };
         cur_ids = mask(cur_ids, 0);
@@ -388,55 +484,50 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       }
       // K or V of tile i into its ring; lane 0 posts the expected bytes, then
       // every box is issued by its own lane.
-      auto issue = [&](int i, bool is_v, bool is_prefix, int page_id) -> bool {
-        const int nst = is_v ? G::kVStages : G::kKStages;
+      auto issue = [&](int i, bool is_prefix, int page_id) -> bool {
+        const int nst = v_warp ? G::kVStages : G::kKStages;
         const int st = i % nst;
-        uint64_t* full = (is_v ? v_full : k_full) + st;
+        uint64_t* full = (v_warp ? v_full : k_full) + st;
         if (i >= nst) {
-          const bool ok = mbar_wait((is_v ? v_empty : k_empty) + st, ((i / nst) - 1) & 1);
+          const bool ok = mbar_wait((v_warp ? v_empty : k_empty) + st, ((i / nst) - 1) & 1);
           if (!__all_sync(0xffffffffu, ok)) return false;
         }
-        if (lane == 0) mbar_arrive_expect_tx(full, uint32_t(G::kHalfTile / parts));
+        if (lane == 0) mbar_arrive_expect_tx(full, uint32_t(G::kHalfTile));
         __syncwarp();
         if (lane < per_part) {
-          const int box = part * per_part + lane;
-          const int j = box / KB;    // page of the tile
-          const int kb = box % KB;   // 64-dim block
-          uint8_t* dst = smem + (is_v ? G::kVOff : G::kKOff) + st * G::kHalfTile +
+          const int j = lane / KB;   // page of the tile
+          const int kb = lane % KB;  // 64-dim block
+          uint8_t* dst = smem + (v_warp ? G::kVOff : G::kKOff) + st * G::kHalfTile +
                          kb * (kTreeTile * 128) + j * 2048;
           if (is_prefix) {
-            tma_load_4d(dst, is_v ? &vmap : &kmap, full, kb * 64, kvh, 0, page_id);
+            tma_load_4d(dst, v_warp ? &vmap : &kmap, full, kb * 64, kvh, 0, page_id);
           } else {
             const int slot = (t * 4 + j) * 16;  // draft slot of this box
             const int rq = slot / npad, nb = slot % npad;
             const int b = rq < nreq ? b0 + rq : p.batch;  // past the block: zeros
-            tma_load_4d(dst, is_v ? &dvmap : &dkmap, full, kb * 64, kvh, nb, b);
+            tma_load_4d(dst, v_warp ? &dvmap : &dkmap, full, kb * 64, kvh, nb, b);
           }
         }
         __syncwarp();
         return true;
       };
-      for (int i = 0; i < ntiles; ++i) {
-        if (i > 0 && (i & 7) == 0) {
+      for (int j = 0, i = psub; i < ntiles; ++j, i += 2) {
+        if (j > 0 && (j & 7) == 0) {
           cur_ids = next_ids;
-          next_ids = load_ids(i + 8);
+          next_ids = load_ids(j + 8);
         }
         const bool is_prefix = run < nruns;
         // the page id of this lane's box
-        const int page_id = __shfl_sync(0xffffffffu, cur_ids,
-                                        (i & 7) * 4 + min((part * per_part + lane) / KB, 3));
+        const int page_id = __shfl_sync(0xffffffffu, cur_ids, (j & 7) * 4 + min(lane / KB, 3));
         if (!v_warp && is_prefix && lane < 4 * KB && lane % KB == 0 &&
             (page_id >= p.physical_pages || page_id < -1))
           atomicOr(p.err, kErrPageRange);
-        if (!issue(i, v_warp, is_prefix, page_id)) {
+        if (!issue(i, is_prefix, page_id)) {
           if (lane == 0) atomicOr(p.err, kErrTimeout);
           break;
         }
-        ++t;
-        while (run < nruns && t >= run_tiles[run]) {  // empty runs have no tiles
-          t -= run_tiles[run];
-          ++run;
-        }
+        step();
+        step();
       }
     }
   } else if (warp == 9) {
@@ -506,8 +597,22 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       if (!mbar_wait(pv_fin, 0)) atomicOr(p.err, kErrTimeout);
     }
   }
+  // ---- epilogue of warps 8-15: the barriers of the softmax warps' epilogue,
+  // the TMEM release, and a share of the owners' sums.
+  grid_launch_dependents();
+  if (to_cluster) cluster_sync_all();
+  tc_fence_before();
+  named_barrier_sync(1, kTreeThreads);  // every TMEM read is done
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tbase, G::kTmemCols);
+  }
+  if (to_cluster) merge_owned_rows();
+  return;
+  }
 
   // ------------------------------------------------------------ softmax rows
+  regs_increase<kTreeSoftmaxRegs>();
   float m_ref = kNegInf, l_sum = 0.f;
   const int wg = warp >> 2;                 // softmax group (warps 0-7)
   const int r = (warp & 3) * 32 + lane;     // row of the tile = TMEM lane
@@ -680,32 +785,11 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // The next kernel of the stream may be scheduled (it waits for this grid).
   grid_launch_dependents();
   // Wait for the last PV, then each row thread of group 0 reads its O rows.
-  const bool to_cluster = p.splits > 1;
-  const int csize = p.splits;
-  const uint32_t rank = to_cluster ? cluster_ctarank() : 0u;
-  const int rpk = (kTreeRows + csize - 1) / csize;  // rows owned by each CTA of the cluster
-  const int valid_rows = min(kTreeRows, nreq * p.rows_req - trow * kTreeRows);
-  auto out_ptr = [&](int row) -> size_t {
-    const int br = trow * kTreeRows + row;
-    const int rq = br / p.rows_req, node = (br % p.rows_req) / p.group, hh = br % p.group;
-    return ((size_t(b0 + rq) * p.nodes + node) * p.hq + size_t(kvh) * p.group + hh) * D;
-  };
-  auto store_out4 = [&](size_t base, float a, float b, float c, float d) {
-    if constexpr (OUT_HALF) {
-      uint2 v;
-      v.x = pack_half2(a, b);
-      v.y = pack_half2(c, d);
-      *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.out) + base) = v;
-    } else {
-      *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + base) = make_float4(a, b, c, d);
-    }
-  };
   // The two groups exchange their per-row (m, l) through shared memory, so
   // every softmax thread knows its row's merged state; warps w and w+4 share
   // TMEM lanes (rows) and each moves one half of the row's D columns.
   float* ml_x = reinterpret_cast<float*>(smem + G::kMlXOff);  // [group][row][m, l]
   float* cl_ml = reinterpret_cast<float*>(smem + G::kWg1Off);  // [row][m, l], read by peers
-  int* orow = reinterpret_cast<int*>(smem + G::kORowOff);
   constexpr int kHalfD = D / 2;
   const int col0 = wg * kHalfD;  // this thread's columns of O
   bool have = false;
@@ -760,8 +844,6 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       }
     }
   }
-  // Rows of this tile owned by this CTA in the cluster merge.
-  const int own_rows = to_cluster ? max(0, min(rpk, valid_rows - int(rank) * rpk)) : 0;
   if (to_cluster && tid == 0 && own_rows > 0)  // armed before any peer can send
     mbar_arrive_expect_tx(recv_done, uint32_t((csize - 1) * own_rows * G::kRowBytes));
   if (to_cluster) {
@@ -803,11 +885,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     for (int e = 0; e < kHalfD; e += 4) store_out4(base + e, f[e], f[e + 1], f[e + 2], f[e + 3]);
   }
   tc_fence_before();
-  __syncthreads();
-  if (warp == 9) {
-    tc_fence_after();
-    tmem_dealloc(tbase, G::kTmemCols);
-  }
+  named_barrier_sync(1, kTreeThreads);  // every TMEM read is done (warp 9 frees TMEM)
   if (to_cluster) {
     // Send every peer the rows it owns (one bulk copy each, completing on
     // the peer's barrier), then sum the received slots of this CTA's own rows
@@ -824,43 +902,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
             smem_u32(smem + G::kStageOff + k * rpk * G::kRowBytes),
             uint32_t(rows_k * G::kRowBytes), map_to_rank(smem_u32(recv_done), uint32_t(k)));
     }
-    bool got = true;
-    if (own_rows > 0) got = mbar_wait(recv_done, 0);
-    // Every row this CTA owns has arrived, so every copy into it is done:
-    // announce that now, and wait for the peers only before leaving.
-    cluster_arrive_relaxed();
-    if (!got) {
-      if (tid == 0) atomicOr(p.err, kErrTimeout);
-    } else {
-      const int row0 = int(rank) * rpk;
-      for (int task = tid; task < own_rows * (D / 4); task += kTreeThreads) {
-        const int rl = task / (D / 4), chunk = task % (D / 4);
-        const int row = row0 + rl;
-        const int off = ((chunk ^ (row & 7)) << 4);
-        float4 v[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          if (c < csize) {
-            const uint8_t* src = c == int(rank)
-                                     ? smem + G::kStageOff + row * G::kRowBytes
-                                     : smem + G::kKOff + (c * rpk + rl) * G::kRowBytes;
-            v[c] = *reinterpret_cast<const float4*>(src + off);
-          }
-        }
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);  // rank order: deterministic
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          if (c < csize) {
-            acc.x += v[c].x;
-            acc.y += v[c].y;
-            acc.z += v[c].z;
-            acc.w += v[c].w;
-          }
-        }
-        store_out4(size_t(orow[row]) * D + chunk * 4, acc.x, acc.y, acc.z, acc.w);
-      }
-    }
-    cluster_wait();  // no CTA leaves while its staged rows may still be read
+    merge_owned_rows();
   }
 }
 

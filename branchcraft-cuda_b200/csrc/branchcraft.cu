@@ -288,9 +288,16 @@ template <int D, bool PREC, bool OUT_HALF>
 cudaError_t configure_tree_kernel(int dev) {
   static std::atomic<uint64_t> configured{0};
   if (configured.load(std::memory_order_relaxed) & (uint64_t(1) << dev)) return cudaSuccess;
+  // The kernel's register split (setmaxnreg) hands out exactly the launch
+  // budget of kTreeLaunchRegs per thread; with fewer registers at launch its
+  // increase could never be granted, so such a build is refused here.
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, tree_mma_kernel<D, PREC, OUT_HALF>);
+  if (e != cudaSuccess) return e;
+  if (fa.numRegs != kTreeLaunchRegs) return cudaErrorInvalidDeviceFunction;
   const size_t most = TreeGeom<D, PREC>::smem_bytes(BC_MAX_NODES);
-  cudaError_t e = cudaFuncSetAttribute(tree_mma_kernel<D, PREC, OUT_HALF>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, int(most));
+  e = cudaFuncSetAttribute(tree_mma_kernel<D, PREC, OUT_HALF>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, int(most));
   if (e != cudaSuccess) return e;
   configured.fetch_or(uint64_t(1) << dev);
   return cudaSuccess;
