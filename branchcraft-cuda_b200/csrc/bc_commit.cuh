@@ -23,8 +23,10 @@ __global__ void __launch_bounds__(256)
                   const int* __restrict__ req, const int* __restrict__ path,
                   const int* __restrict__ dest_pages, const int* __restrict__ dest_slots,
                   int request, unsigned* err) {
-  grid_dependency_wait();  // the preceding kernel of the stream has finished
+  // The next kernel may be scheduled at once (one wave: it only waits, on
+  // free SMs, for this grid to finish).
   grid_launch_dependents();
+  grid_dependency_wait();  // the preceding kernel of the stream has finished
   const int e = blockIdx.x;
   const int r = req ? req[e] : request;
   const int node = path[e];
@@ -61,8 +63,8 @@ __global__ void __launch_bounds__(256)
     clone_kernel(int page_halves, int physical_pages, __half* cache_k, __half* cache_v,
                  const int* __restrict__ src_pages, const int* __restrict__ dst_pages,
                  unsigned* err) {
-  grid_dependency_wait();
   grid_launch_dependents();
+  grid_dependency_wait();
   const int c = blockIdx.y;
   const int src = src_pages[c], dst = dst_pages[c];
   if (src < 0 || src >= physical_pages || dst < 0 || dst >= physical_pages) {

@@ -57,15 +57,19 @@ constexpr int kTreeKStages = 5;
 constexpr int kTreeVStages = 8;
 constexpr int kTreeThreads = 512;   // 8 softmax warps, 4 TMA producers, S issuer, PV issuer, 2 idle
 // Registers: launched at 128 per thread (65,536 / 512); after the prologue
-// the softmax warpgroups grow to 160 and the other two shrink to 96
-// (2 x 128 x 160 + 2 x 128 x 96 = 65,536: the whole launch budget; both
-// paths compile without spills at these budgets).
+// the softmax warpgroups grow and the other two shrink by the same amount
+// (2 x 128 x (softmax + other) = 65,536: the whole launch budget). The
+// splits are the ones at which both paths compile without spills.
 constexpr int kTreeLaunchRegs = 128;
-constexpr int kTreeSoftmaxRegs = 160;
-constexpr int kTreeOtherRegs = 96;
-static_assert(2 * 128 * kTreeSoftmaxRegs + 2 * 128 * kTreeOtherRegs ==
-                  kTreeThreads * kTreeLaunchRegs,
-              "the register split must use exactly the launch budget");
+template <int D>
+struct TreeRegs {
+  static constexpr int kSoftmax = D == 128 ? 168 : 144;
+  static constexpr int kOther = 2 * kTreeLaunchRegs - kSoftmax;
+  static_assert(2 * 128 * (kSoftmax + kOther) == kTreeThreads * kTreeLaunchRegs,
+                "the register split must use exactly the launch budget");
+  static_assert(kSoftmax % 8 == 0 && kOther % 8 == 0 && kOther >= 24 && kSoftmax <= 256,
+                "setmaxnreg takes multiples of 8 in [24, 256]");
+};
 constexpr int kTreeMaxReq = 128;     // requests per CTA (rows per request >= 1)
 
 struct TreeParams {
@@ -76,6 +80,7 @@ struct TreeParams {
   int tiles_per_block;  // row tiles per request block
   int blocks;           // ceil(batch / R)
   int splits;           // CTAs of a cluster along the keys (gridDim.z)
+  int early_trigger;    // the grid is one wave: let the next kernel be scheduled at once
   const __half* q;      // [B, N, Hq, D]
   const int* pages;
   const int* lengths;
@@ -102,10 +107,13 @@ struct TreeGeom {
   static constexpr int kORowOff = kWg1Off + kTreeRows * 8;  // [128] output row of each tile row
   static constexpr int kMlXOff = kORowOff + kTreeRows * 4;  // [2][128][2] each group's (m, l)
   static constexpr int kParOff = kMlXOff + 2 * kTreeRows * 8;
-  // Cluster merge (after the main loop, reusing the K/V rings):
-  // kSlotRows received rows [source rank][row] at kKOff, then this CTA's own
-  // 128 weighted rows (16-byte chunks XOR-swizzled by row) at kStageOff.
-  static constexpr int kRowBytes = D * 4;
+  // Epilogue (after the main loop, reusing the K/V rings): this CTA's 128
+  // output rows at kStageOff, each D FP32 values and a 16-byte trailer
+  // holding the row's (m, l) for the cluster merge; for a cluster split,
+  // kSlotRows received rows [source rank][row] at kKOff. The odd number of
+  // 16-byte units per row spreads a warp's row-per-thread writes over all
+  // banks.
+  static constexpr int kRowBytes = D * 4 + 16;
   static constexpr int kSlotRows = 136;  // >= csize * ceil(128 / csize), csize <= 8
   static constexpr int kStageOff = kKOff + kSlotRows * kRowBytes;
   static_assert(kStageOff + kTreeRows * kRowBytes <= kBarOff,
@@ -213,6 +221,9 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // is bounded per issuing warp).
   const bool producer = warp == 8 || warp == 10 || warp == 12 || warp == 14;
   const int psub = warp >= 12 ? 1 : 0;  // tile parity of a producer warp
+  // A one-wave grid lets the next kernel of the stream be scheduled now: its
+  // CTAs take free SMs, run their set-up and wait there for this grid.
+  if (p.early_trigger) grid_launch_dependents();
   grid_dependency_wait();  // inputs written by the preceding kernel are visible
 
   // ---- prologue. Every global load of the prologue (lengths, parent rows,
@@ -408,25 +419,40 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       for (int task = tid; task < own_rows * (D / 4); task += kTreeThreads) {
         const int rl = task / (D / 4), chunk = task % (D / 4);
         const int row = row0 + rl;
-        const int off = ((chunk ^ (row & 7)) << 4);
-        float4 v[8];
+        // slot c: rank c's copy of the row (this CTA's own from its staging)
+        auto slot = [&](int c) -> const uint8_t* {
+          return c == int(rank) ? smem + G::kStageOff + row * G::kRowBytes
+                                : smem + G::kKOff + (c * rpk + rl) * G::kRowBytes;
+        };
+        float2 ml[8];
+        float M = kNegInf;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           if (c < csize) {
-            const uint8_t* src = c == int(rank)
-                                     ? smem + G::kStageOff + row * G::kRowBytes
-                                     : smem + G::kKOff + (c * rpk + rl) * G::kRowBytes;
-            v[c] = *reinterpret_cast<const float4*>(src + off);
+            ml[c] = *reinterpret_cast<const float2*>(slot(c) + D * 4);
+            M = fmaxf(M, ml[c].x);
           }
         }
+        // Weight of rank c: exp2(m_c - M) / L (0 for a rank without keys).
+        float L = 0.f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          if (c < csize) {
+            ml[c].x = ml[c].x != kNegInf ? fast_exp2(ml[c].x - M) : 0.f;
+            L += ml[c].x * ml[c].y;
+          }
+        }
+        const float inv = L > 0.f ? 1.f / L : 0.f;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);  // rank order: deterministic
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           if (c < csize) {
-            acc.x += v[c].x;
-            acc.y += v[c].y;
-            acc.z += v[c].z;
-            acc.w += v[c].w;
+            const float4 v = *reinterpret_cast<const float4*>(slot(c) + chunk * 16);
+            const float wgt = ml[c].x * inv;
+            acc.x += wgt * v.x;
+            acc.y += wgt * v.y;
+            acc.z += wgt * v.z;
+            acc.w += wgt * v.w;
           }
         }
         store_out4(size_t(orow[row]) * D + chunk * 4, acc.x, acc.y, acc.z, acc.w);
@@ -439,7 +465,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // the softmax warpgroups. The two paths never rejoin (this one returns after
   // its share of the epilogue), so each is compiled to its own budget.
   if (warp >= 8) {
-  regs_decrease<kTreeOtherRegs>();
+  regs_decrease<TreeRegs<D>::kOther>();
   if (producer) {
     // ------------------------------------------------------------ producers
     // warps 8 / 12: K, warps 10 / 14: V; tiles of parity psub
@@ -612,7 +638,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   }
 
   // ------------------------------------------------------------ softmax rows
-  regs_increase<kTreeSoftmaxRegs>();
+  regs_increase<TreeRegs<D>::kSoftmax>();
   float m_ref = kNegInf, l_sum = 0.f;
   const int wg = warp >> 2;                 // softmax group (warps 0-7)
   const int r = (warp & 3) * 32 + lane;     // row of the tile = TMEM lane
@@ -784,112 +810,97 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // ------------------------------------------------------------ epilogue
   // The next kernel of the stream may be scheduled (it waits for this grid).
   grid_launch_dependents();
-  // Wait for the last PV, then each row thread of group 0 reads its O rows.
-  // The two groups exchange their per-row (m, l) through shared memory, so
-  // every softmax thread knows its row's merged state; warps w and w+4 share
-  // TMEM lanes (rows) and each moves one half of the row's D columns.
+  // Wait for the last PV; the two groups exchange their per-row (m, l)
+  // through shared memory, so every softmax thread knows its row's merged
+  // state; warps w and w+4 share TMEM lanes (rows) and each moves one half of
+  // the row's D columns into the staging rows (the K/V rings are idle now).
   float* ml_x = reinterpret_cast<float*>(smem + G::kMlXOff);  // [group][row][m, l]
-  float* cl_ml = reinterpret_cast<float*>(smem + G::kWg1Off);  // [row][m, l], read by peers
   constexpr int kHalfD = D / 2;
   const int col0 = wg * kHalfD;  // this thread's columns of O
-  bool have = false;
-  float w0 = 0.f, w1 = 0.f, mm = kNegInf;
-  float f[kHalfD];  // this thread's part of the row: w0 * O0 + w1 * O1
-  if (warp < 8) {
-    have = ntiles > wg && softmax_ok;
+  {
+    const bool have = ntiles > wg && softmax_ok;
     const int last = have ? wg + 2 * ((ntiles - 1 - wg) / 2) : 0;
+    bool ok = have;
     if (have && !mbar_wait(&pv_done[last & 1], (last >> 1) & 1)) {
-      have = false;
+      ok = false;
       if (lane == 0) atomicOr(p.err, kErrTimeout);
     }
-    ml_x[(wg * kTreeRows + r) * 2 + 0] = have ? m_ref : kNegInf;
-    ml_x[(wg * kTreeRows + r) * 2 + 1] = have ? l_sum : 0.f;
-    named_barrier_sync(2, 256);
-    const float m0 = ml_x[r * 2 + 0], l0 = ml_x[r * 2 + 1];
-    const float m1 = ml_x[(kTreeRows + r) * 2 + 0], l1 = ml_x[(kTreeRows + r) * 2 + 1];
-    mm = fmaxf(m0, m1);
-    // A group contributes only if its max is finite (it saw a valid key).
-    const bool use0 = m0 != kNegInf, use1 = m1 != kNegInf;
-    w0 = use0 ? fast_exp2(m0 - mm) : 0.f;
-    w1 = use1 ? fast_exp2(m1 - mm) : 0.f;
-    const float lsum = w0 * l0 + w1 * l1;
-    if (to_cluster) {
-      if (wg == 0) {
-        cl_ml[r * 2 + 0] = mm;
-        cl_ml[r * 2 + 1] = lsum;
-      }
-    } else {
-      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-      w0 *= inv;
-      w1 *= inv;
-    }
-    // O from TMEM (before the cluster barrier: the loads overlap its wait).
-    // The reads are warp-collective: they depend only on whether the group
-    // processed any tile at all (uniform across the warp).
-    tc_fence_after();
+    ml_x[(wg * kTreeRows + r) * 2 + 0] = ok ? m_ref : kNegInf;
+    ml_x[(wg * kTreeRows + r) * 2 + 1] = ok ? l_sum : 0.f;
+  }
+  named_barrier_sync(2, 256);
+  const float m0 = ml_x[r * 2 + 0], l0 = ml_x[r * 2 + 1];
+  const float m1 = ml_x[(kTreeRows + r) * 2 + 0], l1 = ml_x[(kTreeRows + r) * 2 + 1];
+  const float mm = fmaxf(m0, m1);
+  // A group contributes only if its max is finite (it saw a valid key).
+  const bool use0 = m0 != kNegInf, use1 = m1 != kNegInf;
+  float w0 = use0 ? fast_exp2(m0 - mm) : 0.f;
+  float w1 = use1 ? fast_exp2(m1 - mm) : 0.f;
+  const float lsum = w0 * l0 + w1 * l1;
+  uint8_t* srow = smem + G::kStageOff + r * G::kRowBytes;
+  if (to_cluster) {
+    // Unnormalised rows travel with their (m, l): the owner weighs them.
+    if (wg == 0) *reinterpret_cast<float4*>(srow + D * 4) = make_float4(mm, lsum, 0.f, 0.f);
+  } else {
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    w0 *= inv;
+    w1 *= inv;
+  }
+  if (wg == 0 && r < valid_rows) orow[r] = int(out_ptr(r) / D);
+  // O from TMEM: both groups' accumulators for this thread's columns, one
+  // wait for all four loads. The reads are warp-collective: they depend only
+  // on whether the group processed any tile at all (uniform across the warp).
+  tc_fence_after();
+  {
     const bool read0 = ntiles > 0, read1 = ntiles > 1;
+    uint32_t oa[kHalfD / 32][32], ob[kHalfD / 32][32];
 #pragma unroll
     for (int h = 0; h < kHalfD / 32; ++h) {
-      uint32_t o[32], o1[32];
-      if (read0) tmem_ld32(tbase + lane_addr + G::kTmemO + col0 + 32 * h, o);
-      if (read1) tmem_ld32(tbase + lane_addr + G::kTmemO + 128 + col0 + 32 * h, o1);
-      tmem_ld_wait();
-      if (read0) tmem_bind32(o);
-      if (read1) tmem_bind32(o1);
+      if (read0) tmem_ld32(tbase + lane_addr + G::kTmemO + col0 + 32 * h, oa[h]);
+      if (read1) tmem_ld32(tbase + lane_addr + G::kTmemO + 128 + col0 + 32 * h, ob[h]);
+    }
+    tmem_ld_wait();
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float a = (read0 && use0) ? w0 * __uint_as_float(o[e]) : 0.f;
-        const float b = (read1 && use1) ? w1 * __uint_as_float(o1[e]) : 0.f;
-        f[32 * h + e] = a + b;
+    for (int h = 0; h < kHalfD / 32; ++h) {
+      if (read0) tmem_bind32(oa[h]);
+      if (read1) tmem_bind32(ob[h]);
+    }
+    const float u0 = (read0 && use0) ? w0 : 0.f, u1 = (read1 && use1) ? w1 : 0.f;
+#pragma unroll
+    for (int h = 0; h < kHalfD / 32; ++h) {
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        float4 v;
+        v.x = (read0 ? u0 * __uint_as_float(oa[h][e + 0]) : 0.f) + (read1 ? u1 * __uint_as_float(ob[h][e + 0]) : 0.f);
+        v.y = (read0 ? u0 * __uint_as_float(oa[h][e + 1]) : 0.f) + (read1 ? u1 * __uint_as_float(ob[h][e + 1]) : 0.f);
+        v.z = (read0 ? u0 * __uint_as_float(oa[h][e + 2]) : 0.f) + (read1 ? u1 * __uint_as_float(ob[h][e + 2]) : 0.f);
+        v.w = (read0 ? u0 * __uint_as_float(oa[h][e + 3]) : 0.f) + (read1 ? u1 * __uint_as_float(ob[h][e + 3]) : 0.f);
+        *reinterpret_cast<float4*>(srow + (col0 + 32 * h + e) * 4) = v;
       }
     }
   }
-  if (to_cluster && tid == 0 && own_rows > 0)  // armed before any peer can send
-    mbar_arrive_expect_tx(recv_done, uint32_t((csize - 1) * own_rows * G::kRowBytes));
   if (to_cluster) {
-    cluster_sync_all();  // every CTA's (m, l) is final and its rings are idle
-    if (warp < 8) {
-      float share = 0.f;
-      if (r < valid_rows) {
-        const uint32_t ml_addr = smem_u32(cl_ml + r * 2);
-        float2 mlc[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          if (c < csize) mlc[c] = ld_cluster_f32x2(map_to_rank(ml_addr, uint32_t(c)));
-        float M = kNegInf;
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          if (c < csize) M = fmaxf(M, mlc[c].x);
-        float L = 0.f;
-        if (M != kNegInf) {
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            if (c < csize && mlc[c].x != kNegInf) L += fast_exp2(mlc[c].x - M) * mlc[c].y;
-        }
-        // This CTA's share of the row: exp2(mm - M) / L (0 for a CTA without keys).
-        share = (mm != kNegInf && L > 0.f) ? fast_exp2(mm - M) / L : 0.f;
-        if (wg == 0) orow[r] = int(out_ptr(r) / D);
-        uint8_t* srow = smem + G::kStageOff + r * G::kRowBytes;
-#pragma unroll
-        for (int e = 0; e < kHalfD; e += 4) {
-          const int chunk = (col0 + e) >> 2;
-          *reinterpret_cast<float4*>(srow + ((chunk ^ (r & 7)) << 4)) =
-              make_float4(f[e] * share, f[e + 1] * share, f[e + 2] * share, f[e + 3] * share);
-        }
-      }
-      fence_proxy_async_smem();  // staged rows -> the bulk copies
+    fence_proxy_async_smem();  // staged rows -> the bulk copies
+    if (tid == 0 && own_rows > 0)  // armed before any peer can send
+      mbar_arrive_expect_tx(recv_done, uint32_t((csize - 1) * own_rows * G::kRowBytes));
+    cluster_sync_all();  // every CTA's rows are staged and its rings are idle
+  } else {
+    // Coalesced stores: consecutive threads write consecutive 16-byte
+    // pieces of a row (a thread per row would touch a line per store).
+    named_barrier_sync(2, 256);
+    for (int task = tid; task < valid_rows * (D / 4); task += 256) {
+      const int row = task / (D / 4), chunk = task % (D / 4);
+      const float4 v = *reinterpret_cast<const float4*>(smem + G::kStageOff +
+                                                        row * G::kRowBytes + chunk * 16);
+      store_out4(size_t(orow[row]) * D + chunk * 4, v.x, v.y, v.z, v.w);
     }
-  } else if (warp < 8 && r < valid_rows) {
-    const size_t base = out_ptr(r) + col0;
-#pragma unroll
-    for (int e = 0; e < kHalfD; e += 4) store_out4(base + e, f[e], f[e + 1], f[e + 2], f[e + 3]);
   }
   tc_fence_before();
   named_barrier_sync(1, kTreeThreads);  // every TMEM read is done (warp 9 frees TMEM)
   if (to_cluster) {
-    // Send every peer the rows it owns (one bulk copy each, completing on
-    // the peer's barrier), then sum the received slots of this CTA's own rows
-    // in rank order and store them.
+    // Send every peer the rows it owns with their (m, l) (one bulk copy
+    // each, completing on the peer's barrier), then sum the received slots of
+    // this CTA's own rows in rank order and store them.
     // (warp k sends peer k's rows: copies issued by different warps proceed
     // in parallel)
     if (lane == 0 && warp < csize && warp != int(rank)) {

@@ -355,6 +355,9 @@ cudaError_t launch_tree_t(TreeParams& p, const CUtensorMap* maps, int items, int
   cudaError_t e = configure_tree_kernel<D, PREC, OUT_HALF>(dev);
   if (e != cudaSuccess) return e;
   p.splits = tree_splits<D, PREC, OUT_HALF>(dev, items, tiles);
+  // One CTA per SM: a cluster split fits one wave by construction, an
+  // unsplit grid when it has no more CTAs than SMs.
+  p.early_trigger = (p.splits > 1 || items <= sm_count(dev)) ? 1 : 0;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(items), 1, unsigned(p.splits));
   cfg.blockDim = dim3(kTreeThreads, 1, 1);
