@@ -59,11 +59,12 @@ constexpr int kTreeThreads = 512;   // 8 softmax warps, 4 TMA producers, S issue
 // Registers: launched at 128 per thread (65,536 / 512); after the prologue
 // the softmax warpgroups grow and the other two shrink by the same amount
 // (2 x 128 x (softmax + other) = 65,536: the whole launch budget). The
-// splits are the ones at which both paths compile without spills.
+// splits are the ones with the fewest spills (none at D=64, one register's
+// worth at D=128).
 constexpr int kTreeLaunchRegs = 128;
 template <int D>
 struct TreeRegs {
-  static constexpr int kSoftmax = D == 128 ? 168 : 144;
+  static constexpr int kSoftmax = D == 128 ? 160 : 144;
   static constexpr int kOther = 2 * kTreeLaunchRegs - kSoftmax;
   static_assert(2 * 128 * (kSoftmax + kOther) == kTreeThreads * kTreeLaunchRegs,
                 "the register split must use exactly the launch budget");
@@ -406,59 +407,58 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   const int own_rows = to_cluster ? max(0, min(rpk, valid_rows - int(rank) * rpk)) : 0;
   // The cluster merge's last step, shared by all 512 threads: wait for the
   // peers' rows, sum each owned row's slots in rank order and store it.
+  // The owners' sums run on the softmax warps (tid < 256); warps 8-15 only
+  // take part in the cluster barrier.
   auto merge_owned_rows = [&]() {
-    bool got = true;
-    if (own_rows > 0) got = mbar_wait(recv_done, 0);
-    // Every row this CTA owns has arrived, so every copy into it is done:
-    // announce that now, and wait for the peers only before leaving.
-    cluster_arrive_relaxed();
-    if (!got) {
-      if (tid == 0) atomicOr(p.err, kErrTimeout);
-    } else {
-      const int row0 = int(rank) * rpk;
-      for (int task = tid; task < own_rows * (D / 4); task += kTreeThreads) {
-        const int rl = task / (D / 4), chunk = task % (D / 4);
-        const int row = row0 + rl;
-        // slot c: rank c's copy of the row (this CTA's own from its staging)
-        auto slot = [&](int c) -> const uint8_t* {
-          return c == int(rank) ? smem + G::kStageOff + row * G::kRowBytes
-                                : smem + G::kKOff + (c * rpk + rl) * G::kRowBytes;
-        };
-        float2 ml[8];
-        float M = kNegInf;
+    const uint32_t stage = smem_u32(smem + G::kStageOff);
+    const int row0 = int(rank) * rpk;
+    for (int task = tid; task < own_rows * (D / 4); task += 256) {
+      const int rl = task / (D / 4), chunk = task % (D / 4);
+      const int row = row0 + rl;
+      // this row in every rank's staging area, through the cluster window
+      const uint32_t here = stage + uint32_t(row * G::kRowBytes);
+      // Every rank's (m, l) and piece of the row, all loads in flight at once.
+      float2 ml[8];
+      float4 v[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          if (c < csize) {
-            ml[c] = *reinterpret_cast<const float2*>(slot(c) + D * 4);
-            M = fmaxf(M, ml[c].x);
-          }
+      for (int c = 0; c < 8; ++c) {
+        if (c < csize) {
+          const uint32_t there = map_to_rank(here, uint32_t(c));
+          ml[c] = ld_cluster_f32x2(there + D * 4);
+          v[c] = ld_cluster_f32x4(there + chunk * 16);
         }
-        // Weight of rank c: exp2(m_c - M) / L (0 for a rank without keys).
-        float L = 0.f;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          if (c < csize) {
-            ml[c].x = ml[c].x != kNegInf ? fast_exp2(ml[c].x - M) : 0.f;
-            L += ml[c].x * ml[c].y;
-          }
-        }
-        const float inv = L > 0.f ? 1.f / L : 0.f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);  // rank order: deterministic
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          if (c < csize) {
-            const float4 v = *reinterpret_cast<const float4*>(slot(c) + chunk * 16);
-            const float wgt = ml[c].x * inv;
-            acc.x += wgt * v.x;
-            acc.y += wgt * v.y;
-            acc.z += wgt * v.z;
-            acc.w += wgt * v.w;
-          }
-        }
-        store_out4(size_t(orow[row]) * D + chunk * 4, acc.x, acc.y, acc.z, acc.w);
       }
+      float M = kNegInf;
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        if (c < csize) M = fmaxf(M, ml[c].x);
+      // Weight of rank c: exp2(m_c - M) / L (0 for a rank without keys).
+      float L = 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        if (c < csize) {
+          ml[c].x = ml[c].x != kNegInf ? fast_exp2(ml[c].x - M) : 0.f;
+          L += ml[c].x * ml[c].y;
+        }
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);  // rank order: deterministic
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        if (c < csize) {
+          const float wgt = ml[c].x * inv;
+          acc.x += wgt * v[c].x;
+          acc.y += wgt * v[c].y;
+          acc.z += wgt * v[c].z;
+          acc.w += wgt * v[c].w;
+        }
+      }
+      store_out4(size_t(orow[row]) * D + chunk * 4, acc.x, acc.y, acc.z, acc.w);
     }
-    cluster_wait();  // no CTA leaves while its staged rows may still be read
+    // This CTA's reads of its peers' rows are done; no CTA leaves while its
+    // staged rows may still be read.
+    cluster_arrive_relaxed();
+    cluster_wait();
   };
 
   // Warps 8-15 (producers, MMA issuers, two idle warps) give up registers to
@@ -633,7 +633,10 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     tc_fence_after();
     tmem_dealloc(tbase, G::kTmemCols);
   }
-  if (to_cluster) merge_owned_rows();
+  if (to_cluster) {  // the softmax warps' cluster barrier after their sums
+    cluster_arrive_relaxed();
+    cluster_wait();
+  }
   return;
   }
 
@@ -880,10 +883,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     }
   }
   if (to_cluster) {
-    fence_proxy_async_smem();  // staged rows -> the bulk copies
-    if (tid == 0 && own_rows > 0)  // armed before any peer can send
-      mbar_arrive_expect_tx(recv_done, uint32_t((csize - 1) * own_rows * G::kRowBytes));
-    cluster_sync_all();  // every CTA's rows are staged and its rings are idle
+    cluster_sync_all();  // every CTA's rows are staged (and readable by its peers)
   } else {
     // Coalesced stores: consecutive threads write consecutive 16-byte
     // pieces of a row (a thread per row would touch a line per store).
@@ -897,24 +897,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   }
   tc_fence_before();
   named_barrier_sync(1, kTreeThreads);  // every TMEM read is done (warp 9 frees TMEM)
-  if (to_cluster) {
-    // Send every peer the rows it owns with their (m, l) (one bulk copy
-    // each, completing on the peer's barrier), then sum the received slots of
-    // this CTA's own rows in rank order and store them.
-    // (warp k sends peer k's rows: copies issued by different warps proceed
-    // in parallel)
-    if (lane == 0 && warp < csize && warp != int(rank)) {
-      const int k = warp;
-      const int rows_k = min(rpk, valid_rows - k * rpk);
-      if (rows_k > 0)
-        bulk_copy_to_peer(
-            map_to_rank(smem_u32(smem + G::kKOff) + uint32_t(int(rank) * rpk * G::kRowBytes),
-                        uint32_t(k)),
-            smem_u32(smem + G::kStageOff + k * rpk * G::kRowBytes),
-            uint32_t(rows_k * G::kRowBytes), map_to_rank(smem_u32(recv_done), uint32_t(k)));
-    }
-    merge_owned_rows();
-  }
+  if (to_cluster) merge_owned_rows();
 }
 
 }  // namespace bc
