@@ -62,8 +62,8 @@ SCALE = 1.0 / math.sqrt(128.0)
 # --batch 64 (266,106 tokens) and is scaled by tokens to the 256-request batch
 # (1,142,306 tokens): its traffic is a per-token stream.
 NCU_TRAFFIC = {
-    "tree-cow": 9172480,
-    "tree-scale": 1881058816 + 514093056,
+    "tree-cow": 9176320,
+    "tree-scale": 1880360000 + 514063872,
     "decode": 2147777536 + 7383040,
     "packed": round((1092800512 + 7438080) * 1142306 / 266106),
 }
