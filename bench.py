@@ -534,6 +534,89 @@ class TreeOracle(TreeCow):
         return time.perf_counter() - t, self.step_bytes, 1
 
 
+class TreeHbm(TreeCow):
+    """Tree verify where every request has its own prefix (no sharing): 256
+    requests x 2040-token private prefixes, 7-node random trees (config-2
+    shapes), FP32 output. Not a BASELINE config: it shows the verifier
+    against the HBM roofline on a workload large enough to be bandwidth-bound
+    (2.1 GB of K/V per step, two rotating copies: inputs larger than L2)."""
+
+    name = "tree-hbm"
+
+    def __init__(self, torch, C, device, rank, world, batch=0, **_):
+        from bc_workloads import rand_half, random_parents
+
+        self.torch, self.C, self.device = torch, C, device
+        B = batch or 256
+        rng = np.random.default_rng(4096 + rank)
+        prefix, N, npg = 2040, 7, 128
+        self.batch, self.N, self.nodes, self.prefix = B, N, N, prefix
+        P = B * npg + 8
+        self.pages = rng.permutation(P).astype(np.int32)[:B * npg].reshape(B, npg)
+        self.lengths = np.full(B, prefix, np.int32)
+        self.dq = rand_half(rng, (B, N, 32, 128))
+        self.dk = rand_half(rng, (B, N, 8, 128))
+        self.dv = rand_half(rng, (B, N, 8, 128))
+        self.parent = np.stack([random_parents(rng, N) for _ in range(B)]).astype(np.int32)
+        self.shape = C.make_shape(B, 32, 8, 128, npg, P)
+        self.P = P
+        self.io_arrays = {"draft_q": self.dq, "draft_k": self.dk, "draft_v": self.dv,
+                          "parent": self.parent, "pages": self.pages, "lengths": self.lengths}
+        self.out_shape = (B, N, 32, 128)
+        self.out_dtype = torch.float32
+        self.launches = 1
+        self.step_bytes = (B * prefix * 4096 + 2 * B * N * 8 * 128 * 2 + B * N * 32 * 128 * 2
+                           + B * N * 32 * 128 * 4 + B * npg * 4 + B * 4 + B * N * 4)
+        self.kernel_bytes = self.step_bytes
+        self.kernel = "tree_mma_kernel (tree_verify, private prefixes)"
+        self.bound = "hbm"
+        self._make_copies(None, None)
+
+    def _make_copies(self, k0, v0):
+        torch = self.torch
+        self.copies = 2  # 4.2 GB of K/V in all, far above L2
+        g = torch.Generator(device=self.device)
+        g.manual_seed(11)
+        shape = (self.P, 16, 8, 128)
+        self.caches = [(torch.randn(shape, device=self.device, dtype=torch.float16, generator=g),
+                        torch.randn(shape, device=self.device, dtype=torch.float16, generator=g))
+                       for _ in range(self.copies)]
+        self.ios = [PackedInputs(torch, self.io_arrays, self.device) for _ in range(self.copies)]
+        self.outs = [torch.empty(self.out_shape, dtype=self.out_dtype, device=self.device)
+                     for _ in range(self.copies)]
+        self.out_hosts = [torch.empty(self.out_shape, dtype=self.out_dtype).pin_memory()
+                          for _ in range(self.copies)]
+        self.rot = 0
+
+    def config(self):
+        return {"workload": f"tree_verify, {self.batch} requests x {self.prefix}-token private "
+                            "prefixes (no sharing), 7-node random trees, FP32 output (not a "
+                            "BASELINE config: the verifier on an HBM-bound workload)",
+                "step_bytes": self.step_bytes}
+
+    def cpu_baseline(self):
+        O = oracle_module()
+        torch = self.torch
+        ck, cv = self.caches[0]
+        ids = torch.from_numpy(self.pages[0].astype(np.int64)).to(self.device)
+        k = half_bits(torch, ck[ids])
+        v = half_bits(torch, cv[ids])
+        pages = np.arange(self.pages.shape[1], dtype=np.int32).reshape(1, -1)
+        s = (1, 32, 8, 128, pages.shape[1], pages.shape[1])
+        t = time.perf_counter()
+        O.tree(s, self.N, self.dq[:1], k, v, pages, self.lengths[:1], self.dk[:1], self.dv[:1],
+               self.parent[:1], threads=O.max_threads())
+        dt = time.perf_counter() - t
+        per_step = dt * self.batch
+        return {"value": self.step_bytes / per_step / 1e12, "unit": self.unit,
+                "cores": O.max_threads(), "kind": "port",
+                "sample": f"request 0 of {self.batch}, scaled linearly to the batch",
+                "seconds": round(dt, 4)}
+
+    def reference_step(self, pool):
+        return None
+
+
 class Decode:
     """paged split-KV decode of `batch` one-token requests
     over `context` tokens each (pages in a seeded random permutation)."""
@@ -906,7 +989,7 @@ class LongCtx:
         return None
 
 
-WORKLOADS = {w.name: w for w in (TreeCow, TreeOracle, Decode, Packed, TreeScale, LongCtx)}
+WORKLOADS = {w.name: w for w in (TreeCow, TreeOracle, TreeHbm, Decode, Packed, TreeScale, LongCtx)}
 
 
 # --------------------------------------------------------------- our arm

@@ -100,7 +100,7 @@ struct TreeGeom {
   static constexpr int kKOff = 0;
   static constexpr int kVOff = kKOff + kKStages * kHalfTile;
   static constexpr int kBarOff = kVOff + kVStages * kHalfTile;
-  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 3 + 3 + 2 + 2 + 1 + 1 + 1;
+  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 3 + 3 + 3 + 2 + 1 + 1 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   // misc: tmem base (4) + nruns (4) + run tables 6 x kTreeMaxReq ints
   static constexpr int kRunOff = kMiscOff + 16;
@@ -150,8 +150,12 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   uint64_t* v_full = k_empty + G::kKStages;         // [kVStages]
   uint64_t* v_empty = v_full + G::kVStages;
   uint64_t* s_full = v_empty + G::kVStages;         // [3] per S/P buffer
-  uint64_t* p_full = s_full + G::kSBufs;       // [2] per softmax group
-  uint64_t* pv_done = p_full + 2;              // [2]
+  // P written, per S/P buffer (not per softmax group: a group may finish its
+  // next tile before the PV issuer looks, and a barrier two phases ahead of
+  // its waiter reads as not yet complete; per buffer, the next arrival needs
+  // S(i + 3), hence PV(i), hence the waiter's pass).
+  uint64_t* p_full = s_full + G::kSBufs;       // [3]
+  uint64_t* pv_done = p_full + G::kSBufs;      // [2] per softmax group (O rescale)
   uint64_t* mma_done = pv_done + 2;            // [1] the S issuer's last MMA
   uint64_t* s_free = mma_done + 1;             // [3] PV done reading S/P buffer b
   uint64_t* pv_fin = s_free + G::kSBufs;       // [1] the PV issuer's last MMA
@@ -198,12 +202,10 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     for (int s = 0; s < G::kSBufs; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 1);
+      mbar_init(&p_full[s], 4);
     }
     mbar_init(pv_fin, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&p_full[s], 4);
-      mbar_init(&pv_done[s], 1);
-    }
+    for (int s = 0; s < 2; ++s) mbar_init(&pv_done[s], 1);
     mbar_init(mma_done, 1);
     mbar_init(recv_done, 1);
     fence_mbar_init();
@@ -596,7 +598,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         const int vst = i % G::kVStages;
         const int buf = i & 1;
         const int sb = i % G::kSBufs;
-        if (!mbar_wait(&p_full[buf], (i >> 1) & 1) ||
+        if (!mbar_wait(&p_full[sb], (i / G::kSBufs) & 1) ||
             !mbar_wait(&v_full[vst], (i / G::kVStages) & 1)) {
           ok = false;
           break;
@@ -800,7 +802,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       tmem_st_wait();  // P (and a rescaled O) are in TMEM before the MMA reads them
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[buf]);
+      if (lane == 0) mbar_arrive(&p_full[sb]);
       t += 2;  // the other group takes the tile in between
       while (run < nruns && t >= run_tiles[run]) {  // empty runs have no tiles
         t -= run_tiles[run];
@@ -821,10 +823,12 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   constexpr int kHalfD = D / 2;
   const int col0 = wg * kHalfD;  // this thread's columns of O
   {
+    // Every PV has completed once the PV issuer's final commit lands: a
+    // single-phase barrier (a group's own pv_done may still be two phases
+    // behind its last tile here, which its parity cannot tell apart).
     const bool have = ntiles > wg && softmax_ok;
-    const int last = have ? wg + 2 * ((ntiles - 1 - wg) / 2) : 0;
     bool ok = have;
-    if (have && !mbar_wait(&pv_done[last & 1], (last >> 1) & 1)) {
+    if (have && !mbar_wait(pv_fin, 0)) {
       ok = false;
       if (lane == 0) atomicOr(p.err, kErrTimeout);
     }

@@ -76,6 +76,38 @@ def test_random_trees(capi, batch, prefix, nodes, hq, hkv, dim):
     assert U.max_abs(got, expected) < 2e-4
 
 
+def test_private_prefixes_more_ctas_than_sms(capi):
+    """80 requests with private 2040-token prefixes: 4 runs per CTA and 160
+    CTAs, more than one wave on 148 SMs. Matches the oracle, and 400 launches
+    back to back (programmatic dependent launches, with the softmax groups
+    free to run ahead of the PV issuer) leave the device error word clear and
+    the output bit-identical (this shape once exposed a barrier-phase
+    aliasing stall)."""
+    rng = np.random.default_rng(80)
+    f = _tree_fixture(rng, 80, 2040, 7, shared=False)
+    expected = _oracle_tree(f, 7)
+    s = capi.make_shape(*f["shape"])
+    t = {n: U.to_dev(f[n]) for n in ("draft_q", "k", "v", "pages", "lengths", "draft_k",
+                                     "draft_v", "parent")}
+    out = torch.full(t["draft_q"].shape, float("nan"), device="cuda")
+
+    def run():
+        capi.tree_verify(s, t["draft_q"], t["k"], t["v"], t["pages"], t["lengths"],
+                         t["draft_k"], t["draft_v"], t["parent"], out, 7)
+
+    capi.last_device_error()
+    run()
+    torch.cuda.synchronize()
+    first = out.cpu().numpy()
+    U.assert_close_baseline(first, expected)
+    assert U.max_abs(first, expected) < 2e-4
+    for _ in range(400):
+        run()
+    torch.cuda.synchronize()
+    assert capi.last_device_error() == 0
+    assert np.array_equal(out.cpu().numpy(), first)
+
+
 def test_baseline_config1_fp16_output(capi):
     """1 request, 2048-token prefix in a seeded permutation of a 256-page pool,
     parents [-1,0,0,1,1,2,2], FP16 output checked at the BASELINE tolerance."""
