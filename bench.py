@@ -1137,7 +1137,7 @@ def run_ours(args):
             cb = wl.cpu_baseline()
             cb["value"] = float(f"{cb['value']:.6g}")
             line["cpu_baseline"] = cb
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         import torch.distributed as dist
 
@@ -1152,12 +1152,12 @@ def run_reference(args):
         return
     O = oracle_module()
     if not O.ref_available():
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libbcref.so (the "
-                                                            "reference built from its sources) is missing"}))
+        emit({"impl": "reference", "unavailable": "oracle/_ref/libbcref.so (the reference "
+                                                 "built from its sources) is missing"})
         return
     if args.workload not in ("tree-cow", "tree-oracle", "decode"):
-        print(json.dumps({"impl": "reference", "unavailable": f"no reference CPU path measured "
-                                                            f"for workload {args.workload}"}))
+        emit({"impl": "reference", "unavailable": f"no reference CPU path measured "
+                                                 f"for workload {args.workload}"})
         return
     from concurrent.futures import ThreadPoolExecutor
 
@@ -1174,8 +1174,8 @@ def run_reference(args):
         unit = TreeCow.unit
     else:
         if device is None:
-            print(json.dumps({"impl": "reference", "unavailable": "this workload's inputs are "
-                                                                "generated on a GPU"}))
+            emit({"impl": "reference", "unavailable": "this workload's inputs are "
+                                                     "generated on a GPU"})
             return
         import bc_capi as C
 
@@ -1195,7 +1195,7 @@ def run_reference(args):
                 break
     total = sum(times)
     value = bytes_ / total / 1e12 if unit == "TB/s" else units / total
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": METRIC, "value": float(f"{value:.6g}"), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / len(times) * 1e3, 3), "steps_timed": len(times),
@@ -1212,7 +1212,15 @@ def run_reference(args):
                                    "a bounded slice of the step, scaled linearly"},
         "e2e": {"value": float(f"{value:.6g}"), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
+
+
+RESULT_OUT = sys.stdout
+
+
+def emit(line):
+    """Print the run's one JSON line on the real standard output."""
+    print(json.dumps(line), file=RESULT_OUT, flush=True)
 
 
 def main():
@@ -1235,6 +1243,12 @@ def main():
         args.steps = {"tree-cow": 2000, "tree-oracle": 2000}.get(args.workload, 50)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
+    # stdout carries exactly the one JSON line: anything else written to file
+    # descriptor 1 (library banners such as NCCL's version line) goes to stderr.
+    global RESULT_OUT
+    RESULT_OUT = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
     else:
