@@ -285,7 +285,9 @@ class TreeCow:
         self.out_shape = (wl.batch, wl.nodes, wl.hq, wl.dim)
         self.out_dtype = torch.float32
         self.nodes = wl.nodes
-        self.launches = 1 + bool(plan.clone_src) + bool(plan.entry_node)
+        ncl, nent = len(plan.clone_src), len(plan.entry_node)
+        # tree verify + one commit launch (two beyond 256 clones)
+        self.launches = 1 + (0 if ncl + nent == 0 else 1 if ncl <= 256 else 1 + bool(nent))
         self.step_bytes = wl.verify_bytes() + wl.commit_bytes(plan)
         self.kernel_bytes = wl.verify_bytes()
         self.kernel = "tree_mma_kernel (tree_verify)"

@@ -620,8 +620,8 @@ int bc_commit_batch(const bc_shape* s, int nodes, const void* draft_k, const voi
   if (!err) return cudaErrorInvalidDevice;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int row = s->kv_heads * s->dim;
-  // Both launches are programmatic dependents of the kernel before them: the
-  // clones wait for the preceding kernel, the row writes for the clones.
+  // Programmatic dependent launches: scheduled while the kernel before them
+  // finishes, waiting for it before the first read.
   cudaLaunchAttribute pdl[1];
   pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   pdl[0].val.programmaticStreamSerializationAllowed = 1;
@@ -630,6 +630,16 @@ int bc_commit_batch(const bc_shape* s, int nodes, const void* draft_k, const voi
   cfg.stream = st;
   cfg.attrs = pdl;
   cfg.numAttrs = 1;
+  if (nclones + nentries == 0) return cudaSuccess;
+  if (nclones <= 256) {  // one launch (each entry CTA lists at most 256 clones)
+    cfg.gridDim = dim3(unsigned(8 * nclones + nentries), 1, 1);
+    return cudaLaunchKernelEx(&cfg, commit_batch_kernel, row, s->batch, nodes, s->physical_pages,
+                              static_cast<const __half*>(draft_k),
+                              static_cast<const __half*>(draft_v), static_cast<__half*>(cache_k),
+                              static_cast<__half*>(cache_v), clone_src, clone_dst, nclones,
+                              entry_request, entry_node, entry_page, entry_slot, nentries, err);
+  }
+  // Larger batches: every clone, then every row commit.
   if (nclones > 0) {
     cfg.gridDim = dim3(4, unsigned(nclones), 2);
     cudaError_t e = cudaLaunchKernelEx(&cfg, clone_kernel, 16 * row, s->physical_pages,

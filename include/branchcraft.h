@@ -110,9 +110,13 @@ int bc_commit_path(const bc_shape* shape, const void* draft_k, const void* draft
 /* A whole batch of copy-on-write commits in one call: first every page clone
  * cache[clone_dst[c]] = cache[clone_src[c]] (K and V, all 16 slots), then every
  * entry cache[entry_page[e], entry_slot[e]] = draft[entry_request[e],
- * entry_node[e]]. All index arrays are device arrays. Not in the reference; it
- * is the device half of PagedTreeCache.commit
- * (python/branchcraft_torch/transaction.py:114-150) for many requests. */
+ * entry_node[e]]. All index arrays are device arrays; clone destinations are
+ * distinct pages that are neither clone sources nor written by two entries at
+ * the same slot. One kernel launch for up to 256 clones (the bytes each clone
+ * and entry touch are partitioned, so the clones-first order needs no
+ * ordering between CTAs), two beyond. Not in the reference; it is the device
+ * half of PagedTreeCache.commit (python/branchcraft_torch/transaction.py:114-150)
+ * for many requests. */
 int bc_commit_batch(const bc_shape* shape, int nodes, const void* draft_k,
                     const void* draft_v, void* cache_k, void* cache_v, const int* clone_src,
                     const int* clone_dst, int nclones, const int* entry_request,

@@ -105,3 +105,36 @@ def test_commit_batch_bit_exact(capi):
     assert np.array_equal(U.half_bits(tk), exp_k)
     assert np.array_equal(U.half_bits(tv), exp_v)
     assert capi.last_device_error() == 0
+
+
+def test_commit_batch_many_clones(capi):
+    """300 clones of one page (beyond the one-launch limit of 256: every clone,
+    then every row commit), an in-place commit into the cloned page and rows
+    into some of the clones; bit-exact against clones-first, then commits."""
+    rng = np.random.default_rng(5)
+    P, hkv, dim, B, N = 320, 2, 64, 4, 3
+    ck = U.rand_half(rng, (P, 16, hkv, dim))
+    cv = U.rand_half(rng, (P, 16, hkv, dim))
+    dk = U.rand_half(rng, (B, N, hkv, dim))
+    dv = U.rand_half(rng, (B, N, hkv, dim))
+    clone_src = np.full(300, 7, np.int32)
+    clone_dst = np.arange(10, 310, dtype=np.int32)
+    req = np.array([0, 1, 2, 3], np.int32)
+    node = np.array([0, 1, 2, 0], np.int32)
+    page = np.array([7, 10, 11, 309], np.int32)
+    slot = np.array([8, 8, 9, 15], np.int32)
+    exp_k, exp_v = ck.copy(), cv.copy()
+    for a, b in zip(clone_src, clone_dst):
+        exp_k[b] = exp_k[a]
+        exp_v[b] = exp_v[a]
+    for e in range(len(req)):
+        O.commit(exp_k, exp_v, dk, dv, node[e:e + 1], page[e:e + 1], slot[e:e + 1], int(req[e]))
+    tk, tv = U.to_dev(ck), U.to_dev(cv)
+    s = capi.make_shape(B, hkv, hkv, dim, 1, P)
+    capi.commit_batch(s, N, U.to_dev(dk), U.to_dev(dv), tk, tv, U.to_dev(clone_src),
+                      U.to_dev(clone_dst), U.to_dev(req), U.to_dev(node), U.to_dev(page),
+                      U.to_dev(slot))
+    torch.cuda.synchronize()
+    assert np.array_equal(U.half_bits(tk), exp_k)
+    assert np.array_equal(U.half_bits(tv), exp_v)
+    assert capi.last_device_error() == 0
