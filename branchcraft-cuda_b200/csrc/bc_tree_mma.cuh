@@ -14,9 +14,9 @@
 // Per 64-token tile:  S = Q K^T  (UMMA 128x64x16, FP16 in, FP32 in TMEM),
 // softmax on S (one thread per row, reads its TMEM lane), P (FP16; FP32-exact
 // output uses P = hi + lo and two MMAs) written back over S in TMEM, O += P V
-// (UMMA 128xDx16, V as an MN-major operand) accumulating in TMEM. Q and P are
-// A operands read from tensor memory, so shared memory carries only the K/V
-// tiles: per tile the tensor cores read K once and V once per P part.
+// (UMMA 128xDx16, V as an MN-major operand) accumulating in TMEM. Q is an
+// A operand in shared memory (staged once per CTA), P one in tensor memory:
+// per tile the tensor cores read Q and K once and V once per P part.
 //
 // Warp roles (512 threads): two softmax warpgroups (warps 0-3 and 4-7) take
 // alternate key tiles, each with its own online-softmax state and its own O
@@ -32,9 +32,9 @@
 // registers from the other two (setmaxnreg). K and V tiles stream through
 // separate rings: a K stage is released as soon as its S = Q K^T has been
 // computed, a V stage once its P V product is done, so the copies of later
-// tiles are not held back by the softmax of earlier ones (5 K stages, 8 V
-// stages). Three S/P buffers in TMEM let S be computed two tiles ahead of PV,
-// so a group's next S is ready when its softmax ends.
+// tiles are not held back by the softmax of earlier ones (5 K stages, 6 V
+// stages). Four S/P buffers in TMEM let S be computed up to three tiles ahead
+// of PV, so a group's next S is ready when its softmax ends.
 //
 // The running max is kept lazily: O and l are rescaled only when a row's max
 // grows by more than 2^8 (rare after the first tile), with probabilities up
@@ -54,7 +54,7 @@ namespace bc {
 constexpr int kTreeRows = 128;
 constexpr int kTreeTile = 64;        // keys per tile = 4 pages
 constexpr int kTreeKStages = 5;
-constexpr int kTreeVStages = 8;
+constexpr int kTreeVStages = 6;
 constexpr int kTreeThreads = 512;   // 8 softmax warps, 4 TMA producers, S issuer, PV issuer, 2 idle
 // Registers: launched at 128 per thread (65,536 / 512); after the prologue
 // the softmax warpgroups grow and the other two shrink by the same amount
@@ -99,8 +99,13 @@ struct TreeGeom {
   static constexpr int kHalfTile = KB * kTreeTile * 128;    // K or V of one tile
   static constexpr int kKOff = 0;
   static constexpr int kVOff = kKOff + kKStages * kHalfTile;
-  static constexpr int kBarOff = kVOff + kVStages * kHalfTile;
-  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 3 + 3 + 3 + 2 + 1 + 1 + 1;
+  // Q (the A operand of S = Q K^T): 128 rows, K-major, 128-byte swizzle,
+  // [KB][128 rows][128 B] like the K tiles.
+  static constexpr int kQOff = kVOff + kVStages * kHalfTile;
+  static constexpr int kQBytes = KB * kTreeRows * 128;
+  static constexpr int kBarOff = kQOff + kQBytes;
+  static constexpr int kSBufs = 4;  // S/P buffers in TMEM (tile i uses i % 4)
+  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 3 * kSBufs + 2 + 1 + 1 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   // misc: tmem base (4) + nruns (4) + run tables 6 x kTreeMaxReq ints
   static constexpr int kRunOff = kMiscOff + 16;
@@ -117,15 +122,14 @@ struct TreeGeom {
   static constexpr int kRowBytes = D * 4 + 16;
   static constexpr int kSlotRows = 136;  // >= csize * ceil(128 / csize), csize <= 8
   static constexpr int kStageOff = kKOff + kSlotRows * kRowBytes;
-  static_assert(kStageOff + kTreeRows * kRowBytes <= kBarOff,
+  static_assert(kStageOff + kTreeRows * kRowBytes <= kQOff,
                 "cluster merge buffers must fit in the K/V rings");
   // parent rows (anc_rows ints, 16-byte padded) then ancestor sets (32 B each)
   __host__ __device__ static size_t anc_offset(int anc_rows) { return size_t(kParOff) + ((size_t(anc_rows) * 4 + 15) & ~size_t(15)); }
   static size_t smem_bytes(int anc_rows) { return 1024 + anc_offset(anc_rows) + size_t(anc_rows) * 32; }
-  // TMEM columns: three S/P buffers at 0, 64, 128 (tile i uses i % 3), O of
-  // group g at 192 + 128 g, Q at 448.
-  static constexpr int kSBufs = 3;
-  static constexpr uint32_t kTmemO = 192, kTmemQ = 448;
+  // TMEM columns: four S/P buffers at 0, 64, 128, 192, O of group g at
+  // 256 + 128 g (= 512).
+  static constexpr uint32_t kTmemO = 256;
   static constexpr uint32_t kTmemCols = 512;
 };
 
@@ -154,7 +158,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // next tile before the PV issuer looks, and a barrier two phases ahead of
   // its waiter reads as not yet complete; per buffer, the next arrival needs
   // S(i + 3), hence PV(i), hence the waiter's pass).
-  uint64_t* p_full = s_full + G::kSBufs;       // [3]
+  uint64_t* p_full = s_full + G::kSBufs;       // [kSBufs]
   uint64_t* pv_done = p_full + G::kSBufs;      // [2] per softmax group (O rescale)
   uint64_t* mma_done = pv_done + 2;            // [1] the S issuer's last MMA
   uint64_t* s_free = mma_done + 1;             // [3] PV done reading S/P buffer b
@@ -310,14 +314,15 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         __ldg(p.pages + size_t(b0 + i - 1) * p.max_pages + j))
       atomicMin(&mismatch[i], j);
   }
-  if (warp < 4) {  // query rows -> TMEM (the A operand of S = Q K^T)
-    uint32_t (&q0)[32] = *reinterpret_cast<uint32_t (*)[32]>(&qv[0]);
-    tmem_st32(tbase + lane_addr + G::kTmemQ, q0);
-    if constexpr (D == 128) {
-      uint32_t (&q1)[32] = *reinterpret_cast<uint32_t (*)[32]>(&qv[32]);
-      tmem_st32(tbase + lane_addr + G::kTmemQ + 32, q1);
-    }
-    tmem_st_wait();
+  if (warp < 4) {  // query row tid -> shared memory (the A operand of S = Q K^T)
+    // K-major with the 128-byte swizzle the MMA descriptor expects: 16-byte
+    // chunk c of a 64-dim block's row r at (c ^ (r & 7)) * 16.
+    const uint32_t qrow = smem_u32(smem + G::kQOff) + uint32_t(tid) * 128;
+#pragma unroll
+    for (int k = 0; k < D / 8; ++k)
+      st_shared_v4(qrow + (k / 8) * (kTreeRows * 128) + (((k & 7) ^ (tid & 7)) << 4),
+                   qv[4 * k + 0], qv[4 * k + 1], qv[4 * k + 2], qv[4 * k + 3]);
+    fence_proxy_async_smem();  // the rows -> the MMA's reads
   }
   tc_fence_before();
   __syncthreads();
@@ -576,12 +581,13 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         }
         tc_fence_after();
         const uint32_t kbase = k_addr + kst * G::kHalfTile;
+        const uint32_t qbase = smem_u32(smem + G::kQOff);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const int kb = ks >> 2, kin = ks & 3;
+          const uint64_t adesc = umma_desc_sw128(qbase + kb * (kTreeRows * 128) + kin * 32, 16, 1024);
           const uint64_t bdesc = umma_desc_sw128(kbase + kb * (kTreeTile * 128) + kin * 32, 16, 1024);
-          umma_f16_ts(tbase + uint32_t(sb) * 64, tbase + G::kTmemQ + ks * 8, bdesc, kIdescS,
-                      ks > 0 ? 1u : 0u);
+          umma_f16(tbase + uint32_t(sb) * 64, adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sb]);
         umma_commit(&k_empty[kst]);  // K stage free once S is computed
