@@ -191,12 +191,6 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr, uint32_t ran
   return r;
 }
 
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ float2 ld_cluster_f32x2(uint32_t addr) {
   float2 v;
   asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
@@ -210,18 +204,6 @@ __device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
                : "r"(addr)
                : "memory");
   return v;
-}
-
-// Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory into a
-// peer CTA's (both addresses 16-byte aligned), completing on the peer's
-// mbarrier; both remote addresses come from map_to_rank.
-__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, uint32_t src_cta,
-                                                  uint32_t bytes, uint32_t bar_cluster) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
-      "[%3];" ::"r"(dst_cluster),
-      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
-      : "memory");
 }
 
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {

@@ -105,12 +105,11 @@ struct TreeGeom {
   static constexpr int kQBytes = KB * kTreeRows * 128;
   static constexpr int kBarOff = kQOff + kQBytes;
   static constexpr int kSBufs = 4;  // S/P buffers in TMEM (tile i uses i % 4)
-  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 3 * kSBufs + 2 + 1 + 1 + 1;
+  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 3 * kSBufs + 2 + 1 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   // misc: tmem base (4) + nruns (4) + run tables 6 x kTreeMaxReq ints
   static constexpr int kRunOff = kMiscOff + 16;
-  static constexpr int kWg1Off = kRunOff + 6 * kTreeMaxReq * 4;  // [128][2] second group's (m, l)
-  static constexpr int kORowOff = kWg1Off + kTreeRows * 8;  // [128] output row of each tile row
+  static constexpr int kORowOff = kRunOff + 6 * kTreeMaxReq * 4;  // [128] output row of each tile row
   static constexpr int kMlXOff = kORowOff + kTreeRows * 4;  // [2][128][2] each group's (m, l)
   static constexpr int kParOff = kMlXOff + 2 * kTreeRows * 8;
   // Epilogue (after the main loop, reusing the K/V rings): this CTA's 128
@@ -163,7 +162,6 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   uint64_t* mma_done = pv_done + 2;            // [1] the S issuer's last MMA
   uint64_t* s_free = mma_done + 1;             // [3] PV done reading S/P buffer b
   uint64_t* pv_fin = s_free + G::kSBufs;       // [1] the PV issuer's last MMA
-  uint64_t* recv_done = pv_fin + 1;            // [1] cluster merge: rows received
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kMiscOff);
   int* nruns_s = reinterpret_cast<int*>(smem + G::kMiscOff + 4);
   int* run_first = reinterpret_cast<int*>(smem + G::kRunOff);  // first local request
@@ -211,7 +209,6 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     mbar_init(pv_fin, 1);
     for (int s = 0; s < 2; ++s) mbar_init(&pv_done[s], 1);
     mbar_init(mma_done, 1);
-    mbar_init(recv_done, 1);
     fence_mbar_init();
   }
   if (warp == 9) {
