@@ -564,6 +564,11 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     // ------------------------------------------------------------ S issuer
     if (ntiles > 0 && lane == 0) {
       bool ok = true;
+      // Descriptors for Q and K stage 0; the start-address field (bits 0-13,
+      // address >> 4) takes byte offsets >> 4 directly, shared memory being
+      // below 256 KB.
+      const uint64_t qdesc0 = umma_desc_sw128(smem_u32(smem + G::kQOff), 16, 1024);
+      const uint64_t kdesc0 = umma_desc_sw128(k_addr, 16, 1024);
       for (int i = 0; i < ntiles && ok; ++i) {
         const int kst = i % G::kKStages;
         const int sb = i % G::kSBufs;
@@ -577,13 +582,12 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t kbase = k_addr + kst * G::kHalfTile;
-        const uint32_t qbase = smem_u32(smem + G::kQOff);
+        const uint64_t kdesc = kdesc0 + uint64_t((kst * G::kHalfTile) >> 4);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const int kb = ks >> 2, kin = ks & 3;
-          const uint64_t adesc = umma_desc_sw128(qbase + kb * (kTreeRows * 128) + kin * 32, 16, 1024);
-          const uint64_t bdesc = umma_desc_sw128(kbase + kb * (kTreeTile * 128) + kin * 32, 16, 1024);
+          const uint64_t adesc = qdesc0 + uint64_t((kb * (kTreeRows * 128) + kin * 32) >> 4);
+          const uint64_t bdesc = kdesc + uint64_t((kb * (kTreeTile * 128) + kin * 32) >> 4);
           umma_f16(tbase + uint32_t(sb) * 64, adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[sb]);
@@ -597,6 +601,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     // ------------------------------------------------------------ PV issuer
     if (ntiles > 0 && lane == 0) {
       bool ok = true;
+      const uint64_t vdesc0 = umma_desc_sw128(v_addr, kTreeTile * 128, 1024);
       for (int i = 0; i < ntiles && ok; ++i) {
         const int vst = i % G::kVStages;
         const int buf = i & 1;
@@ -607,7 +612,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t vbase = v_addr + vst * G::kHalfTile;
+        const uint64_t vdesc = vdesc0 + uint64_t((vst * G::kHalfTile) >> 4);
         const uint32_t tP = tbase + uint32_t(sb) * 64;                // P hi (+32: lo)
         const uint32_t tO = tbase + G::kTmemO + uint32_t(buf) * 128;  // group buf's O
 #pragma unroll
@@ -615,7 +620,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           // V: MN-major (dims contiguous); 16 keys = two 8-key groups 1024 B apart;
           // the second 64-dim block sits kTreeTile*128 bytes further. P: 16 keys
           // = 8 TMEM columns of FP16 pairs.
-          const uint64_t bdesc = umma_desc_sw128(vbase + kk * 2048, kTreeTile * 128, 1024);
+          const uint64_t bdesc = vdesc + uint64_t((kk * 2048) >> 4);
           umma_f16_ts(tO, tP + kk * 8, bdesc, kIdescPV, (i >= 2 || kk > 0) ? 1u : 0u);
           if (PREC) umma_f16_ts(tO, tP + 32 + kk * 8, bdesc, kIdescPV, 1u);
         }
