@@ -278,6 +278,18 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// True in one lane of the (fully active) warp, the same lane every time: the
+// lane that issues a warp's MMAs and their commits.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Arrive once on `bar` when every tcgen05.mma this thread issued so far is done.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(

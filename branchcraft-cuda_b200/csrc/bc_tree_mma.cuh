@@ -91,37 +91,43 @@ struct TreeParams {
   unsigned* err;
 };
 
-template <int D, bool PREC>
+// DUAL: one CTA runs two consecutive 128-row tiles of a request block over
+// the same key tiles (softmax warpgroup g owns row tile g), so each K/V tile
+// copied into shared memory feeds twice the MMAs: half the L2 -> SM traffic
+// per FLOP, for grids of several waves whose blocks span two row tiles.
+template <int D, bool PREC, bool DUAL = false>
 struct TreeGeom {
   static constexpr int KB = D / 64;                        // 64-wide swizzle blocks
-  static constexpr int kKStages = kTreeKStages;
-  static constexpr int kVStages = kTreeVStages;
+  static constexpr int kRT = DUAL ? 2 : 1;                 // row tiles per CTA
+  static constexpr int kKStages = DUAL ? kTreeKStages - 1 : kTreeKStages;
+  static constexpr int kVStages = DUAL ? kTreeVStages - 1 : kTreeVStages;
   static constexpr int kHalfTile = KB * kTreeTile * 128;    // K or V of one tile
   static constexpr int kKOff = 0;
   static constexpr int kVOff = kKOff + kKStages * kHalfTile;
-  // Q (the A operand of S = Q K^T): 128 rows, K-major, 128-byte swizzle,
-  // [KB][128 rows][128 B] like the K tiles.
+  // Q (the A operand of S = Q K^T): 128 rows per row tile, K-major, 128-byte
+  // swizzle, [KB][128 rows][128 B] like the K tiles; row tile g at g * kQTile.
   static constexpr int kQOff = kVOff + kVStages * kHalfTile;
-  static constexpr int kQBytes = KB * kTreeRows * 128;
+  static constexpr int kQTile = KB * kTreeRows * 128;
+  static constexpr int kQBytes = kRT * kQTile;
   static constexpr int kBarOff = kQOff + kQBytes;
-  static constexpr int kSBufs = 4;  // S/P buffers in TMEM (tile i uses i % 4)
+  static constexpr int kSBufs = 4;  // S/P buffers in TMEM (unit u uses u % 4)
   static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 3 * kSBufs + 2 + 1 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   // misc: tmem base (4) + nruns (4) + run tables 6 x kTreeMaxReq ints
   static constexpr int kRunOff = kMiscOff + 16;
-  static constexpr int kORowOff = kRunOff + 6 * kTreeMaxReq * 4;  // [128] output row of each tile row
-  static constexpr int kMlXOff = kORowOff + kTreeRows * 4;  // [2][128][2] each group's (m, l)
+  static constexpr int kORowOff = kRunOff + 6 * kTreeMaxReq * 4;  // [kRT*128] output row of each tile row
+  static constexpr int kMlXOff = kORowOff + kRT * kTreeRows * 4;  // [2][128][2] each group's (m, l)
   static constexpr int kParOff = kMlXOff + 2 * kTreeRows * 8;
-  // Epilogue (after the main loop, reusing the K/V rings): this CTA's 128
-  // output rows at kStageOff, each D FP32 values and a 16-byte trailer
-  // holding the row's (m, l) for the cluster merge; for a cluster split,
-  // kSlotRows received rows [source rank][row] at kKOff. The odd number of
-  // 16-byte units per row spreads a warp's row-per-thread writes over all
-  // banks.
+  // Epilogue (after the main loop, reusing the K/V rings): this CTA's output
+  // rows at kStageOff, each D FP32 values and a 16-byte trailer holding the
+  // row's (m, l) for the cluster merge; for a cluster split, kSlotRows
+  // received rows [source rank][row] at kKOff (a DUAL CTA is never split).
+  // The odd number of 16-byte units per row spreads a warp's row-per-thread
+  // writes over all banks.
   static constexpr int kRowBytes = D * 4 + 16;
   static constexpr int kSlotRows = 136;  // >= csize * ceil(128 / csize), csize <= 8
-  static constexpr int kStageOff = kKOff + kSlotRows * kRowBytes;
-  static_assert(kStageOff + kTreeRows * kRowBytes <= kQOff,
+  static constexpr int kStageOff = DUAL ? kKOff : kKOff + kSlotRows * kRowBytes;
+  static_assert(kStageOff + kRT * kTreeRows * kRowBytes <= kQOff,
                 "cluster merge buffers must fit in the K/V rings");
   // parent rows (anc_rows ints, 16-byte padded) then ancestor sets (32 B each)
   __host__ __device__ static size_t anc_offset(int anc_rows) { return size_t(kParOff) + ((size_t(anc_rows) * 4 + 15) & ~size_t(15)); }
@@ -132,13 +138,13 @@ struct TreeGeom {
   static constexpr uint32_t kTmemCols = 512;
 };
 
-template <int D, bool PREC, bool OUT_HALF>
+template <int D, bool PREC, bool OUT_HALF, bool DUAL = false>
 __global__ void __launch_bounds__(kTreeThreads, 1)
     tree_mma_kernel(const __grid_constant__ TreeParams p, const __grid_constant__ CUtensorMap kmap,
                     const __grid_constant__ CUtensorMap vmap,
                     const __grid_constant__ CUtensorMap dkmap,
                     const __grid_constant__ CUtensorMap dvmap) {
-  using G = TreeGeom<D, PREC>;
+  using G = TreeGeom<D, PREC, DUAL>;
   constexpr int KB = G::KB;
   constexpr float kNegInf = -INFINITY;
   constexpr uint32_t kIdescS = umma_idesc_f16(kTreeRows, kTreeTile, false, false);
@@ -181,7 +187,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
 
   // ---- work unit
   const int item = blockIdx.x;
-  const int trow = item % p.tiles_per_block;          // row tile inside the block
+  // first row tile of this CTA inside the block (DUAL: group g runs trow + g)
+  const int trow = (item % p.tiles_per_block) * G::kRT;
   const int bk = item / p.tiles_per_block;
   const int blk = bk % p.blocks;
   const int kvh = bk / p.blocks;
@@ -251,9 +258,10 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       cmp_b[k] = __ldg(p.pages + size_t(b0 + i - 1) * p.max_pages + j);
     }
   }
-  // Query row r (thread r of warps 0-3) into registers, for TMEM lane r.
+  // Query row r of row tile g (thread 128 g + r of warps 0-3, and 4-7 for a
+  // DUAL CTA) into registers.
   uint32_t qv[D / 2];
-  if (warp < 4) {
+  if (warp < 4 * G::kRT) {
     const int br = trow * kTreeRows + tid;
     const bool ok = br < nreq * p.rows_req;
     const int rq = ok ? br / p.rows_req : 0, node = ok ? (br % p.rows_req) / p.group : 0;
@@ -311,13 +319,14 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         __ldg(p.pages + size_t(b0 + i - 1) * p.max_pages + j))
       atomicMin(&mismatch[i], j);
   }
-  if (warp < 4) {  // query row tid -> shared memory (the A operand of S = Q K^T)
+  if (warp < 4 * G::kRT) {  // query rows -> shared memory (the A operand of S = Q K^T)
     // K-major with the 128-byte swizzle the MMA descriptor expects: 16-byte
     // chunk c of a 64-dim block's row r at (c ^ (r & 7)) * 16.
-    const uint32_t qrow = smem_u32(smem + G::kQOff) + uint32_t(tid) * 128;
+    const int qt = tid / kTreeRows, qr = tid % kTreeRows;
+    const uint32_t qrow = smem_u32(smem + G::kQOff) + uint32_t(qt * G::kQTile + qr * 128);
 #pragma unroll
     for (int k = 0; k < D / 8; ++k)
-      st_shared_v4(qrow + (k / 8) * (kTreeRows * 128) + (((k & 7) ^ (tid & 7)) << 4),
+      st_shared_v4(qrow + (k / 8) * (kTreeRows * 128) + (((k & 7) ^ (qr & 7)) << 4),
                    qv[4 * k + 0], qv[4 * k + 1], qv[4 * k + 2], qv[4 * k + 3]);
     fence_proxy_async_smem();  // the rows -> the MMA's reads
   }
@@ -562,55 +571,64 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ S issuer
-    if (ntiles > 0 && lane == 0) {
+    // The whole warp runs the loop (waits, descriptor arithmetic: warp-uniform
+    // values) and one elected lane issues each MMA and commit: a tcgen05.mma
+    // from a lone lane in divergent code costs its warp several times longer.
+    if (ntiles > 0) {
       bool ok = true;
       // Descriptors for Q and K stage 0; the start-address field (bits 0-13,
       // address >> 4) takes byte offsets >> 4 directly, shared memory being
       // below 256 KB.
       const uint64_t qdesc0 = umma_desc_sw128(smem_u32(smem + G::kQOff), 16, 1024);
       const uint64_t kdesc0 = umma_desc_sw128(k_addr, 16, 1024);
-      for (int i = 0; i < ntiles && ok; ++i) {
+      // Unit u: key tile i = u / kRT against row tile g = u % kRT.
+      for (int u = 0; u < ntiles * G::kRT; ++u) {
+        const int i = DUAL ? (u >> 1) : u;
+        const int g = DUAL ? (u & 1) : 0;
         const int kst = i % G::kKStages;
-        const int sb = i % G::kSBufs;
-        // S/P buffer sb was last used by tile i-3: its PV must have read P.
-        if (i >= G::kSBufs && !mbar_wait(&s_free[sb], ((i - G::kSBufs) / G::kSBufs) & 1)) {
-          ok = false;
-          break;
-        }
-        if (!mbar_wait(&k_full[kst], (i / G::kKStages) & 1)) {
-          ok = false;
-          break;
-        }
+        const int sb = u % G::kSBufs;
+        // S/P buffer sb was last used by unit u-4: its PV must have read P.
+        ok = __all_sync(0xffffffffu, (u < G::kSBufs ||
+                                      mbar_wait(&s_free[sb], ((u - G::kSBufs) / G::kSBufs) & 1)) &&
+                                         (g != 0 || mbar_wait(&k_full[kst], (i / G::kKStages) & 1)));
+        if (!ok) break;
         tc_fence_after();
         const uint64_t kdesc = kdesc0 + uint64_t((kst * G::kHalfTile) >> 4);
+        const uint64_t qdesc = qdesc0 + uint64_t((g * G::kQTile) >> 4);
 #pragma unroll
         for (int ks = 0; ks < D / 16; ++ks) {
           const int kb = ks >> 2, kin = ks & 3;
-          const uint64_t adesc = qdesc0 + uint64_t((kb * (kTreeRows * 128) + kin * 32) >> 4);
+          const uint64_t adesc = qdesc + uint64_t((kb * (kTreeRows * 128) + kin * 32) >> 4);
           const uint64_t bdesc = kdesc + uint64_t((kb * (kTreeTile * 128) + kin * 32) >> 4);
-          umma_f16(tbase + uint32_t(sb) * 64, adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
+          if (elect_one()) umma_f16(tbase + uint32_t(sb) * 64, adesc, bdesc, kIdescS, ks > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[sb]);
-        umma_commit(&k_empty[kst]);  // K stage free once S is computed
+        if (elect_one()) {
+          umma_commit(&s_full[sb]);
+          // K stage free once every row tile's S is computed
+          if (g == G::kRT - 1) umma_commit(&k_empty[kst]);
+        }
+        __syncwarp();
       }
-      if (!ok) atomicOr(p.err, kErrTimeout);
-      umma_commit(mma_done);
-      if (!mbar_wait(mma_done, 0)) atomicOr(p.err, kErrTimeout);
+      if (!ok && lane == 0) atomicOr(p.err, kErrTimeout);
+      if (elect_one()) umma_commit(mma_done);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, mbar_wait(mma_done, 0)) && lane == 0) atomicOr(p.err, kErrTimeout);
     }
   } else if (warp == 11) {
     // ------------------------------------------------------------ PV issuer
-    if (ntiles > 0 && lane == 0) {
+    // (whole warp, one elected lane issuing, as for S)
+    if (ntiles > 0) {
       bool ok = true;
       const uint64_t vdesc0 = umma_desc_sw128(v_addr, kTreeTile * 128, 1024);
-      for (int i = 0; i < ntiles && ok; ++i) {
+      for (int u = 0; u < ntiles * G::kRT; ++u) {
+        const int i = DUAL ? (u >> 1) : u;
+        const int g = DUAL ? (u & 1) : 0;
         const int vst = i % G::kVStages;
-        const int buf = i & 1;
-        const int sb = i % G::kSBufs;
-        if (!mbar_wait(&p_full[sb], (i / G::kSBufs) & 1) ||
-            !mbar_wait(&v_full[vst], (i / G::kVStages) & 1)) {
-          ok = false;
-          break;
-        }
+        const int buf = DUAL ? g : (i & 1);  // the O accumulator (and pv_done) of this unit
+        const int sb = u % G::kSBufs;
+        ok = __all_sync(0xffffffffu, mbar_wait(&p_full[sb], (u / G::kSBufs) & 1) &&
+                                         (g != 0 || mbar_wait(&v_full[vst], (i / G::kVStages) & 1)));
+        if (!ok) break;
         tc_fence_after();
         const uint64_t vdesc = vdesc0 + uint64_t((vst * G::kHalfTile) >> 4);
         const uint32_t tP = tbase + uint32_t(sb) * 64;                // P hi (+32: lo)
@@ -621,16 +639,24 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           // the second 64-dim block sits kTreeTile*128 bytes further. P: 16 keys
           // = 8 TMEM columns of FP16 pairs.
           const uint64_t bdesc = vdesc + uint64_t((kk * 2048) >> 4);
-          umma_f16_ts(tO, tP + kk * 8, bdesc, kIdescPV, (i >= 2 || kk > 0) ? 1u : 0u);
-          if (PREC) umma_f16_ts(tO, tP + 32 + kk * 8, bdesc, kIdescPV, 1u);
+          // (an accumulator's first tile overwrites it)
+          const uint32_t acc = (i >= (DUAL ? 1 : 2) || kk > 0) ? 1u : 0u;
+          if (elect_one()) {
+            umma_f16_ts(tO, tP + kk * 8, bdesc, kIdescPV, acc);
+            if (PREC) umma_f16_ts(tO, tP + 32 + kk * 8, bdesc, kIdescPV, 1u);
+          }
         }
-        umma_commit(&pv_done[buf]);
-        umma_commit(&v_empty[vst]);
-        umma_commit(&s_free[sb]);
+        if (elect_one()) {
+          umma_commit(&pv_done[buf]);
+          if (g == G::kRT - 1) umma_commit(&v_empty[vst]);
+          umma_commit(&s_free[sb]);
+        }
+        __syncwarp();
       }
-      if (!ok) atomicOr(p.err, kErrTimeout);
-      umma_commit(pv_fin);
-      if (!mbar_wait(pv_fin, 0)) atomicOr(p.err, kErrTimeout);
+      if (!ok && lane == 0) atomicOr(p.err, kErrTimeout);
+      if (elect_one()) umma_commit(pv_fin);
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, mbar_wait(pv_fin, 0)) && lane == 0) atomicOr(p.err, kErrTimeout);
     }
   }
   // ---- epilogue of warps 8-15: the barriers of the softmax warps' epilogue,
@@ -655,20 +681,24 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   float m_ref = kNegInf, l_sum = 0.f;
   const int wg = warp >> 2;                 // softmax group (warps 0-7)
   const int r = (warp & 3) * 32 + lane;     // row of the tile = TMEM lane
-  const int brow = trow * kTreeRows + r;
+  // DUAL: group wg owns row tile trow + wg and takes every key tile; else the
+  // groups share the row tile and take alternate key tiles.
+  const int brow = (trow + (DUAL ? wg : 0)) * kTreeRows + r;
   const bool row_valid = warp < 8 && brow < nreq * p.rows_req;
   const int my_req = row_valid ? brow / p.rows_req : -1;
   const int my_node = row_valid ? (brow % p.rows_req) / p.group : 0;
   const uint32_t o_col = G::kTmemO + uint32_t(wg & 1) * 128;  // this group's O in TMEM
   bool softmax_ok = true;
-  if (warp < 8 && ntiles > wg) {
+  const int i0 = DUAL ? 0 : wg, di = DUAL ? 1 : 2;  // this group's key tiles
+  if (warp < 8 && ntiles > i0) {
     int run, t;
-    start_cursor(v0 + wg, run, t);
+    start_cursor(v0 + i0, run, t);
     const uint32_t* my_anc = anc + (size_t(max(my_req, 0)) * p.nodes + my_node) * 8;
-    for (int i = wg; i < ntiles; i += 2) {
-      const int buf = i & 1;            // this group's P barrier and O accumulator
-      const int sb = i % G::kSBufs;     // the S/P buffer of tile i
-      if (!mbar_wait(&s_full[sb], (i / G::kSBufs) & 1)) {
+    for (int i = i0; i < ntiles; i += di) {
+      const int buf = DUAL ? wg : (i & 1);   // this group's O accumulator
+      const int u = DUAL ? 2 * i + wg : i;   // the S/P unit
+      const int sb = u % G::kSBufs;          // its S/P buffer
+      if (!mbar_wait(&s_full[sb], (u / G::kSBufs) & 1)) {
         softmax_ok = false;
         break;
       }
@@ -767,8 +797,9 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       }
       l_sum += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       // Keys past a prefix run's end may hold anything: zero their V rows so
-      // that 0 * V stays 0 in the PV product.
-      if (is_prefix && valid_keys < kTreeTile) {
+      // that 0 * V stays 0 in the PV product. (DUAL: group 0 does it; the
+      // other group's PV of this tile is issued after group 0's.)
+      if (is_prefix && valid_keys < kTreeTile && (!DUAL || wg == 0)) {
         // (the V tile may still be in flight: wait for it before writing)
         const int vst = i % G::kVStages;
         if (!mbar_wait(&v_full[vst], (i / G::kVStages) & 1)) {
@@ -786,11 +817,11 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         fence_proxy_async_smem();
       }
       // O rescale (whole warp when any of its rows needs it), once this
-      // group's previous PV (tile i-2) has completed. (P(i) itself needs no
-      // wait: S(i) completing means every earlier MMA, among them the PV
-      // that last read this S/P buffer, has completed.)
+      // group's previous PV (tile i - di) has completed. (P itself needs no
+      // wait: S of this unit completing means every earlier MMA, among them
+      // the PV that last read this S/P buffer, has completed.)
       if (__any_sync(0xffffffffu, rescale)) {
-        if (i >= 2 && !mbar_wait(&pv_done[buf], ((i - 2) >> 1) & 1)) {
+        if (i >= i0 + di && !mbar_wait(&pv_done[buf], ((i - i0 - di) / di) & 1)) {
           softmax_ok = false;
           break;
         }
@@ -811,7 +842,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sb]);
-      t += 2;  // the other group takes the tile in between
+      t += di;  // (non-DUAL: the other group takes the tile in between)
       while (run < nruns && t >= run_tiles[run]) {  // empty runs have no tiles
         t -= run_tiles[run];
         ++run;
@@ -823,6 +854,58 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // ------------------------------------------------------------ epilogue
   // The next kernel of the stream may be scheduled (it waits for this grid).
   grid_launch_dependents();
+  if constexpr (DUAL) {
+    // Each group holds its own rows' final (m, l) and O (a DUAL CTA is never
+    // split): normalise, stage the rows, then coalesced stores by both
+    // groups. The staging rows reuse the K/V rings, idle once every PV is done.
+    bool ok = ntiles > 0 && softmax_ok;
+    if (ok && !mbar_wait(pv_fin, 0)) {
+      ok = false;
+      if (lane == 0) atomicOr(p.err, kErrTimeout);
+    }
+    const float inv = (ok && m_ref != kNegInf && l_sum > 0.f) ? 1.f / l_sum : 0.f;
+    const int q = wg * kTreeRows + r;  // staged row (output row of tile trow + wg)
+    uint8_t* srow = smem + G::kStageOff + q * G::kRowBytes;
+    if (brow < nreq * p.rows_req) orow[q] = int(out_ptr(q) / D);
+    tc_fence_after();
+    // The TMEM reads are warp-collective; whether they run depends only on
+    // ntiles (uniform across the CTA).
+    const bool read = ntiles > 0;
+#pragma unroll
+    for (int h = 0; h < D / 32; h += 2) {
+      uint32_t oa[32], ob[32];
+      if (read) {
+        tmem_ld32(tbase + lane_addr + G::kTmemO + uint32_t(wg) * 128 + 32 * h, oa);
+        tmem_ld32(tbase + lane_addr + G::kTmemO + uint32_t(wg) * 128 + 32 * (h + 1), ob);
+        tmem_ld_wait();
+        tmem_bind32(oa);
+        tmem_bind32(ob);
+      }
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        const float4 va = read ? make_float4(inv * __uint_as_float(oa[e]), inv * __uint_as_float(oa[e + 1]),
+                                             inv * __uint_as_float(oa[e + 2]), inv * __uint_as_float(oa[e + 3]))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 vb = read ? make_float4(inv * __uint_as_float(ob[e]), inv * __uint_as_float(ob[e + 1]),
+                                             inv * __uint_as_float(ob[e + 2]), inv * __uint_as_float(ob[e + 3]))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(srow + (32 * h + e) * 4) = va;
+        *reinterpret_cast<float4*>(srow + (32 * (h + 1) + e) * 4) = vb;
+      }
+    }
+    named_barrier_sync(2, 256);
+    const int rows_all = nreq * p.rows_req - trow * kTreeRows;  // valid rows from tile trow on
+    for (int task = tid; task < 2 * kTreeRows * (D / 4); task += 256) {
+      const int row = task / (D / 4), chunk = task % (D / 4);
+      if (row >= rows_all) break;  // rows past the block's end (row grows with task)
+      const float4 v = *reinterpret_cast<const float4*>(smem + G::kStageOff +
+                                                        row * G::kRowBytes + chunk * 16);
+      store_out4(size_t(orow[row]) * D + chunk * 4, v.x, v.y, v.z, v.w);
+    }
+    tc_fence_before();
+    named_barrier_sync(1, kTreeThreads);  // every TMEM read is done (warp 9 frees TMEM)
+    return;
+  }
   // Wait for the last PV; the two groups exchange their per-row (m, l)
   // through shared memory, so every softmax thread knows its row's merged
   // state; warps w and w+4 share TMEM lanes (rows) and each moves one half of

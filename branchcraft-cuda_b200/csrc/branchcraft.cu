@@ -284,7 +284,7 @@ cudaError_t paged_decode_core(const bc_shape* s, const void* q, const void* k, c
 
 int pick_mode(int splits) { return splits <= 1 ? kSplitNone : splits <= 8 ? kSplitCluster : kSplitGlobal; }
 
-template <int D, bool PREC, bool OUT_HALF>
+template <int D, bool PREC, bool OUT_HALF, bool DUAL = false>
 cudaError_t configure_tree_kernel(int dev) {
   static std::atomic<uint64_t> configured{0};
   if (configured.load(std::memory_order_relaxed) & (uint64_t(1) << dev)) return cudaSuccess;
@@ -292,11 +292,11 @@ cudaError_t configure_tree_kernel(int dev) {
   // budget of kTreeLaunchRegs per thread; with fewer registers at launch its
   // increase could never be granted, so such a build is refused here.
   cudaFuncAttributes fa;
-  cudaError_t e = cudaFuncGetAttributes(&fa, tree_mma_kernel<D, PREC, OUT_HALF>);
+  cudaError_t e = cudaFuncGetAttributes(&fa, tree_mma_kernel<D, PREC, OUT_HALF, DUAL>);
   if (e != cudaSuccess) return e;
   if (fa.numRegs != kTreeLaunchRegs) return cudaErrorInvalidDeviceFunction;
-  const size_t most = TreeGeom<D, PREC>::smem_bytes(BC_MAX_NODES);
-  e = cudaFuncSetAttribute(tree_mma_kernel<D, PREC, OUT_HALF>,
+  const size_t most = TreeGeom<D, PREC, DUAL>::smem_bytes(BC_MAX_NODES);
+  e = cudaFuncSetAttribute(tree_mma_kernel<D, PREC, OUT_HALF, DUAL>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, int(most));
   if (e != cudaSuccess) return e;
   configured.fetch_or(uint64_t(1) << dev);
@@ -346,15 +346,16 @@ int tree_splits(int dev, long long items, int tiles) {
   return c;
 }
 
-template <int D, bool PREC, bool OUT_HALF>
+template <int D, bool PREC, bool OUT_HALF, bool DUAL>
 cudaError_t launch_tree_t(TreeParams& p, const CUtensorMap* maps, int items, int tiles,
                           size_t smem, cudaStream_t stream) {
-  auto kern = tree_mma_kernel<D, PREC, OUT_HALF>;
+  auto kern = tree_mma_kernel<D, PREC, OUT_HALF, DUAL>;
   const int dev = current_device();
   if (dev < 0) return cudaErrorInvalidDevice;
-  cudaError_t e = configure_tree_kernel<D, PREC, OUT_HALF>(dev);
+  cudaError_t e = configure_tree_kernel<D, PREC, OUT_HALF, DUAL>(dev);
   if (e != cudaSuccess) return e;
-  p.splits = tree_splits<D, PREC, OUT_HALF>(dev, items, tiles);
+  // A DUAL grid has several waves by construction: never split.
+  p.splits = DUAL ? 1 : tree_splits<D, PREC, OUT_HALF>(dev, items, tiles);
   // One CTA per SM: a cluster split fits one wave by construction, an
   // unsplit grid when it has no more CTAs than SMs.
   p.early_trigger = (p.splits > 1 || items <= sm_count(dev)) ? 1 : 0;
@@ -411,7 +412,16 @@ cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix
   p.req_per_block = R;
   p.tiles_per_block = (R * p.rows_req + kTreeRows - 1) / kTreeRows;
   p.blocks = (s->batch + R - 1) / R;
-  const long long items = (long long)s->kv_heads * p.blocks * p.tiles_per_block;
+  long long items = (long long)s->kv_heads * p.blocks * p.tiles_per_block;
+  // Blocks of an even number of row tiles, in a grid of at least two waves
+  // even after pairing: one CTA runs two row tiles over each K/V tile (half
+  // the copies per FLOP). Small grids keep one row tile per CTA and split
+  // the keys instead.
+  const bool dual = p.tiles_per_block % 2 == 0 && items / 2 >= 2LL * sm_count(dev);
+  if (dual) {
+    p.tiles_per_block /= 2;
+    items /= 2;
+  }
   if (items > 0x7fffffffLL) return cudaErrorInvalidValue;
   // Key tiles of one CTA before splitting: prefix tiles plus draft tiles.
   const int npad = (nodes + 15) & ~15;
@@ -435,16 +445,19 @@ cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix
       !encode_draft_map(&maps[3], draft_v, s->dim, s->kv_heads, nodes, s->batch))
     return cudaErrorInvalidValue;
   const int anc_rows = R * nodes;
+  const int it = int(items);
   if (s->dim == 64) {
-    const size_t smem = out_half ? TreeGeom<64, false>::smem_bytes(anc_rows)
-                                 : TreeGeom<64, true>::smem_bytes(anc_rows);
-    return out_half ? launch_tree_t<64, false, true>(p, maps, int(items), tiles, smem, stream)
-                    : launch_tree_t<64, true, false>(p, maps, int(items), tiles, smem, stream);
+    if (dual)
+      return out_half ? launch_tree_t<64, false, true, true>(p, maps, it, tiles, TreeGeom<64, false, true>::smem_bytes(anc_rows), stream)
+                      : launch_tree_t<64, true, false, true>(p, maps, it, tiles, TreeGeom<64, true, true>::smem_bytes(anc_rows), stream);
+    return out_half ? launch_tree_t<64, false, true, false>(p, maps, it, tiles, TreeGeom<64, false>::smem_bytes(anc_rows), stream)
+                    : launch_tree_t<64, true, false, false>(p, maps, it, tiles, TreeGeom<64, true>::smem_bytes(anc_rows), stream);
   }
-  const size_t smem = out_half ? TreeGeom<128, false>::smem_bytes(anc_rows)
-                               : TreeGeom<128, true>::smem_bytes(anc_rows);
-  return out_half ? launch_tree_t<128, false, true>(p, maps, int(items), tiles, smem, stream)
-                  : launch_tree_t<128, true, false>(p, maps, int(items), tiles, smem, stream);
+  if (dual)
+    return out_half ? launch_tree_t<128, false, true, true>(p, maps, it, tiles, TreeGeom<128, false, true>::smem_bytes(anc_rows), stream)
+                    : launch_tree_t<128, true, false, true>(p, maps, it, tiles, TreeGeom<128, true, true>::smem_bytes(anc_rows), stream);
+  return out_half ? launch_tree_t<128, false, true, false>(p, maps, it, tiles, TreeGeom<128, false>::smem_bytes(anc_rows), stream)
+                  : launch_tree_t<128, true, false, false>(p, maps, it, tiles, TreeGeom<128, true>::smem_bytes(anc_rows), stream);
 }
 
 }  // namespace

@@ -159,3 +159,41 @@ def test_mixed_prefix_runs(capi, nodes, hq, hkv):
     U.assert_close_baseline(got, expected)
     assert U.max_abs(got, expected) < 2e-4
     assert capi.last_device_error() == 0
+
+
+@pytest.mark.parametrize("batch,nodes,hq,hkv,dim,out_dtype", [
+    (40, 63, 32, 8, 128, torch.float32),   # 252 rows per request: two row tiles
+    (40, 63, 32, 8, 128, torch.float16),
+    (80, 40, 16, 4, 64, torch.float16),    # 160 rows per request, D = 64
+    (80, 40, 16, 4, 64, torch.float32),
+])
+def test_two_row_tiles_per_cta(capi, batch, nodes, hq, hkv, dim, out_dtype):
+    """Requests of more than 128 rows in a grid of several waves: one CTA runs
+    both row tiles of a request over each K/V tile. Private prefixes of mixed
+    lengths (empty, partial last pages, several tiles) and random trees;
+    repeated launches stay bit-identical with the device error word clear."""
+    rng = np.random.default_rng(batch * 7 + nodes + dim)
+    lens = rng.integers(0, 300, size=batch).astype(np.int32)
+    lens[0], lens[1], lens[2] = 0, 64, 1
+    f = U.paged_fixture(rng, batch, hq, hkv, dim, lens)
+    f["draft_q"] = U.rand_half(rng, (batch, nodes, hq, dim))
+    f["draft_k"] = U.rand_half(rng, (batch, nodes, hkv, dim))
+    f["draft_v"] = U.rand_half(rng, (batch, nodes, hkv, dim))
+    f["parent"] = U.random_tree_parents(rng, batch, nodes)
+    expected = _oracle_tree(f, nodes)
+    capi.last_device_error()
+    got = _run_tree(capi, f["shape"], nodes, f, out_dtype=out_dtype)
+    U.assert_close_baseline(got, expected)
+    if out_dtype == torch.float32:
+        assert U.max_abs(got, expected) < 2e-4
+    assert capi.last_device_error() == 0
+    s = capi.make_shape(*f["shape"])
+    t = {n: U.to_dev(f[n]) for n in ("draft_q", "k", "v", "pages", "lengths", "draft_k",
+                                     "draft_v", "parent")}
+    out = torch.empty(t["draft_q"].shape, device="cuda", dtype=out_dtype)
+    for _ in range(50):
+        capi.tree_verify(s, t["draft_q"], t["k"], t["v"], t["pages"], t["lengths"],
+                         t["draft_k"], t["draft_v"], t["parent"], out, nodes)
+    torch.cuda.synchronize()
+    assert capi.last_device_error() == 0
+    assert np.array_equal(out.float().cpu().numpy(), got)
