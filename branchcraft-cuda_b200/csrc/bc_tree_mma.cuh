@@ -720,7 +720,10 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       bool in_run = false;
       if (is_prefix) {
         valid_keys = min(kTreeTile, run_len[run] - t * kTreeTile);
-        in_run = row_valid && my_req >= run_first[run] && my_req < run_end[run];
+        // Rows past the block's last request (zero queries, never stored)
+        // count as in the run: the warp holding the block's last rows then
+        // takes the unmasked path with the others instead of diverging.
+        in_run = !row_valid || (my_req >= run_first[run] && my_req < run_end[run]);
       }
       // x[c] holds the raw score (masked keys: -inf); the scale (> 0) is
       // applied after the max and inside the exponent's FMA.
