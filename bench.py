@@ -63,7 +63,7 @@ SCALE = 1.0 / math.sqrt(128.0)
 # (1,142,306 tokens): its traffic is a per-token stream.
 NCU_TRAFFIC = {
     "tree-cow": 9176320,
-    "tree-scale": 1880360000 + 514063872,
+    "tree-scale": 1880985000 + 514538240,
     "decode": 2147777536 + 7383040,
     "packed": round((1092800512 + 7438080) * 1142306 / 266106),
 }

@@ -721,9 +721,10 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       if (is_prefix) {
         valid_keys = min(kTreeTile, run_len[run] - t * kTreeTile);
         // Rows past the block's last request (zero queries, never stored)
-        // count as in the run: the warp holding the block's last rows then
-        // takes the unmasked path with the others instead of diverging.
-        in_run = !row_valid || (my_req >= run_first[run] && my_req < run_end[run]);
+        // are masked like that request's rows: the warp holding the block's
+        // last rows then takes one softmax path instead of diverging.
+        const int mreq = row_valid ? my_req : nreq - 1;
+        in_run = mreq >= run_first[run] && mreq < run_end[run];
       }
       // x[c] holds the raw score (masked keys: -inf); the scale (> 0) is
       // applied after the max and inside the exponent's FMA.
