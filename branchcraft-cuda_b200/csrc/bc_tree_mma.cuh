@@ -25,10 +25,10 @@
 // producers of K, warps 10 and 14 those of V (pages of the page table, then
 // draft K/V), each of a pair taking alternate tiles: the copy rate of paged
 // boxes is bounded per issuing warp. Warp 9 allocates TMEM and issues the
-// S = Q K^T MMAs from one thread, warp 11 the O += P V MMAs: a tcgen05.mma
-// costs its issuing thread about as long as a 128x64x16 MMA takes to run, so
-// one issuer per GEMM keeps the tensor pipe fed. Warps 13 and 15 only take
-// part in the epilogue. After the prologue the softmax warpgroups take
+// S = Q K^T MMAs, warp 11 the O += P V MMAs (one elected lane each): a
+// tcgen05.mma holds its issuing thread for about its own run time (48 cycles
+// for a 128x64x16 one), so one issuer per GEMM keeps the tensor pipe fed.
+// Warps 13 and 15 only take part in the epilogue. After the prologue the softmax warpgroups take
 // registers from the other two (setmaxnreg). K and V tiles stream through
 // separate rings: a K stage is released as soon as its S = Q K^T has been
 // computed, a V stage once its P V product is done, so the copies of later
@@ -36,15 +36,20 @@
 // stages). Four S/P buffers in TMEM let S be computed up to three tiles ahead
 // of PV, so a group's next S is ready when its softmax ends.
 //
+// DUAL variant (requests of more than 128 rows, grids of several waves): the
+// CTA runs two row tiles over the same key tiles, softmax warpgroup g owning
+// row tile g and taking every key tile; (key tile, row tile) units go through
+// the S/P buffers in turn, so each K/V tile copied serves twice the MMAs.
+//
 // The running max is kept lazily: O and l are rescaled only when a row's max
 // grows by more than 2^8 (rare after the first tile), with probabilities up
 // to 2^8 — the final O / l is unchanged.
 //
 // Splits of the key range across the CTAs of a cluster are merged through
-// distributed shared memory: the CTAs exchange their per-row (m, l), each
-// scales its own O rows by its share of the final normaliser and stores them
-// into the row's owner CTA (stores need no round trip), and every owner sums
-// its rows' slots in rank order (deterministic) and writes the output.
+// distributed shared memory: every CTA stages its unnormalised rows with
+// their (m, l), and each row's owner CTA reads that row from every rank,
+// weighs the ranks by exp2(m_c - M) / L and sums them in rank order
+// (deterministic) before writing the output.
 #pragma once
 
 #include "bc_attn.cuh"
