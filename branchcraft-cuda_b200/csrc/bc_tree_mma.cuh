@@ -576,9 +576,9 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ S issuer
-    // The whole warp runs the loop (waits, descriptor arithmetic: warp-uniform
-    // values) and one elected lane issues each MMA and commit: a tcgen05.mma
-    // from a lone lane in divergent code costs its warp several times longer.
+    // The whole warp runs the loop (waits, descriptor arithmetic on
+    // warp-uniform values) and one elected lane issues each MMA and commit:
+    // 1-3 % faster on config 5a than the same loop run by lane 0 alone.
     if (ntiles > 0) {
       bool ok = true;
       // Descriptors for Q and K stage 0; the start-address field (bits 0-13,
@@ -826,9 +826,9 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         fence_proxy_async_smem();
       }
       // O rescale (whole warp when any of its rows needs it), once this
-      // group's previous PV (tile i - di) has completed. (P itself needs no
-      // wait: S of this unit completing means every earlier MMA, among them
-      // the PV that last read this S/P buffer, has completed.)
+      // group's previous PV (tile i - di) has completed. (Writing P needs no
+      // wait: this unit's S was issued only after the PV that last read this
+      // S/P buffer had completed.)
       if (__any_sync(0xffffffffu, rescale)) {
         if (i >= i0 + di && !mbar_wait(&pv_done[buf], ((i - i0 - di) / di) & 1)) {
           softmax_ok = false;
