@@ -80,7 +80,8 @@ def load_peaks():
 # --------------------------------------------------------------- clocks
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons every 100 ms in the background;
-    `window(t0, t1)` summarises the samples inside [t0, t1]."""
+    `window(t0, t1)` summarises the samples inside [t0, t1] (with the samples
+    just before and after it when fewer than two fall inside)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -113,9 +114,16 @@ class ClockSampler:
                 self.proc.kill()
 
     def window(self, t0, t1):
-        inside = [p for t, p in self.samples if t0 - 0.05 <= t <= t1 + 0.05]
-        if not inside and self.samples:  # region shorter than a sample period
-            inside = [min(self.samples, key=lambda s: abs(s[0] - (t0 + t1) / 2))[1]]
+        inside = [p for t, p in self.samples if t0 <= t <= t1]
+        bracketing = False
+        if len(inside) < 2 and self.samples:
+            # A region shorter than two sample periods: add the last sample
+            # before it and the first after it, which bound its clocks.
+            before = [s for s in self.samples if s[0] < t0]
+            after = [s for s in self.samples if s[0] > t1]
+            inside = (([max(before, key=lambda s: s[0])[1]] if before else []) + inside +
+                      ([min(after, key=lambda s: s[0])[1]] if after else []))
+            bracketing = True
         if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
 
@@ -132,9 +140,12 @@ class ClockSampler:
             for name, val in zip(names, p[5:9]):
                 if val.lower().startswith("active"):
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": num(inside[0][2]), "reasons": sorted(reasons),
-                "samples": len(inside)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None,
+               "sm_max_mhz": num(inside[0][2]), "reasons": sorted(reasons),
+               "samples": len(inside)}
+        if bracketing:
+            out["bracketing"] = True  # samples just before and after the region
+        return out
 
 
 # --------------------------------------------------------------- helpers
