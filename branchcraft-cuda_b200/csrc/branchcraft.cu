@@ -690,21 +690,30 @@ namespace {
 // cudaGetSymbolAddress returns for the device that is current at the call.
 static __device__ __align__(256) float bc_static_decode_scratch[BC_STATIC_SCRATCH_FLOATS];
 
-float* static_scratch_address(int dev) {
+// The array's device address on `dev` (current), looked up once per device.
+// A failed look-up returns its own error code and clears it from the
+// runtime's last-error slot, so the caller's next cudaGetLastError() does not
+// report it a second time.
+cudaError_t static_scratch_address(int dev, float** out) {
   static std::atomic<float*> cache[kMaxDevices];
   static std::mutex mu;
   float* p = cache[dev].load(std::memory_order_acquire);
-  if (p) return p;
-  std::lock_guard<std::mutex> lock(mu);
-  p = cache[dev].load(std::memory_order_relaxed);
   if (!p) {
-    void* addr = nullptr;
-    if (cudaGetSymbolAddress(&addr, bc_static_decode_scratch) != cudaSuccess || !addr)
-      return nullptr;
-    p = static_cast<float*>(addr);
-    cache[dev].store(p, std::memory_order_release);
+    std::lock_guard<std::mutex> lock(mu);
+    p = cache[dev].load(std::memory_order_relaxed);
+    if (!p) {
+      void* addr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&addr, bc_static_decode_scratch);
+      if (e != cudaSuccess || !addr) {
+        cudaGetLastError();
+        return e != cudaSuccess ? e : cudaErrorInvalidDevice;
+      }
+      p = static_cast<float*>(addr);
+      cache[dev].store(p, std::memory_order_release);
+    }
   }
-  return p;
+  *out = p;
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -722,8 +731,9 @@ int bc_decode_static_scratch(const bc_shape* s, const void* q, const void* k, co
   if (need > BC_STATIC_SCRATCH_FLOATS) return cudaErrorInvalidValue;  // beyond the fixed array
   const int dev = current_device();
   if (dev < 0) return cudaErrorInvalidDevice;
-  float* scratch = static_scratch_address(dev);
-  if (!scratch) return cudaErrorInvalidDevice;
+  float* scratch = nullptr;
+  const cudaError_t e = static_scratch_address(dev, &scratch);
+  if (e != cudaSuccess) return e;
   float* partial_a = scratch;                                  // splits * rows * dim
   float* partial_ml = scratch + (long long)splits * rows * s->dim;  // splits * rows * 2
   return paged_decode_core(s, q, k, v, pages, lengths, output, false,

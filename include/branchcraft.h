@@ -19,6 +19,11 @@
  * commit destinations out of range) never fault: the access is skipped (a
  * page outside the pool reads as zeros) and a bit is set in a per-device error
  * word that bc_last_device_error() returns.
+ *
+ * The library keeps, per device and for the life of the process, the device
+ * addresses of its own `__device__` variables (the error word and the fixed
+ * array of bc_decode_static_scratch). They belong to the device's primary
+ * context: do not use the library on a device across cudaDeviceReset().
  */
 #ifndef BRANCHCRAFT_H_
 #define BRANCHCRAFT_H_

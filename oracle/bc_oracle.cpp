@@ -80,6 +80,17 @@ inline uint16_t f2h(float f) {
   return sign | uint16_t(h);
 }
 
+// h2f of every binary16 pattern, built once: the attention loops convert
+// each K/V element through this table (same values as h2f, no branches).
+const float* h2f_table() {
+  static const std::vector<float> table = [] {
+    std::vector<float> t(65536);
+    for (uint32_t h = 0; h < 65536; ++h) t[h] = h2f(uint16_t(h));
+    return t;
+  }();
+  return table.data();
+}
+
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
 void set_threads(int threads) {
@@ -217,6 +228,7 @@ void bco_decode(const BcoShape* shape, const uint16_t* q, const uint16_t* k,
                 float* out, int threads) {
   const BcoShape s = *shape;
   set_threads(threads);
+  const float* hf = h2f_table();
   const int group = s.query_heads / s.kv_heads;
   const double root = std::sqrt(double(s.dim));
 #pragma omp parallel for schedule(dynamic, 1)
@@ -235,7 +247,7 @@ void bco_decode(const BcoShape* shape, const uint16_t* q, const uint16_t* k,
       const long long phys = pages[size_t(b) * s.max_pages + t / kPage];
       const size_t base = ((size_t(phys) * kPage + t % kPage) * s.kv_heads + kvh) * s.dim;
       double dot = 0;
-      for (int d = 0; d < s.dim; ++d) dot += double(qf[d]) * h2f(k[base + d]);
+      for (int d = 0; d < s.dim; ++d) dot += double(qf[d]) * hf[k[base + d]];
       scores[t] = float(dot / root);
       max_score = std::max(max_score, scores[t]);
     }
@@ -245,7 +257,7 @@ void bco_decode(const BcoShape* shape, const uint16_t* q, const uint16_t* k,
       denom += p;
       const long long phys = pages[size_t(b) * s.max_pages + t / kPage];
       const size_t base = ((size_t(phys) * kPage + t % kPage) * s.kv_heads + kvh) * s.dim;
-      for (int d = 0; d < s.dim; ++d) o[d] += float(p * h2f(v[base + d]));
+      for (int d = 0; d < s.dim; ++d) o[d] += float(p * hf[v[base + d]]);
     }
     if (denom != 0)
       for (int d = 0; d < s.dim; ++d) o[d] /= float(denom);
@@ -274,6 +286,7 @@ int bco_tree(const BcoShape* shape, int nodes, const uint16_t* draft_q,
       }
     }
   set_threads(threads);
+  const float* hf = h2f_table();
   const int group = s.query_heads / s.kv_heads;
   const double root = std::sqrt(double(s.dim));
   const int rows = s.batch * nodes * s.query_heads;
@@ -299,7 +312,7 @@ int bco_tree(const BcoShape* shape, int nodes, const uint16_t* draft_q,
     for (size_t t = 0; t < toks.size(); ++t) {
       const uint16_t* kk = toks[t].draft ? draft_k : k;
       double dot = 0;
-      for (int d = 0; d < s.dim; ++d) dot += double(qf[d]) * h2f(kk[toks[t].base + d]);
+      for (int d = 0; d < s.dim; ++d) dot += double(qf[d]) * hf[kk[toks[t].base + d]];
       sc[t] = dot / root;
       mx = std::max(mx, sc[t]);
     }
@@ -310,7 +323,7 @@ int bco_tree(const BcoShape* shape, int nodes, const uint16_t* draft_q,
       const double p = std::exp(sc[t] - mx);
       denom += p;
       const uint16_t* vv = toks[t].draft ? draft_v : v;
-      for (int d = 0; d < s.dim; ++d) o[d] += float(p * h2f(vv[toks[t].base + d]));
+      for (int d = 0; d < s.dim; ++d) o[d] += float(p * hf[vv[toks[t].base + d]]);
     }
     for (int d = 0; d < s.dim; ++d) o[d] /= float(denom);
   }
@@ -330,6 +343,7 @@ void bco_packed_decode(const BcoShape* shape, const uint16_t* q,
                        float* out_f32, int threads) {
   const BcoShape s = *shape;
   set_threads(threads);
+  const float* hf = h2f_table();
   const int group = s.query_heads / s.kv_heads;
 #pragma omp parallel for schedule(dynamic, 1)
   for (int row = 0; row < s.batch * s.query_heads; ++row) {
@@ -346,7 +360,7 @@ void bco_packed_decode(const BcoShape* shape, const uint16_t* q,
       const long long phys = pages[size_t(b) * s.max_pages + t / kPage];
       const long long off = phys * block_stride + kvh * head_stride + (t % kPage) * slot_stride;
       double dot = 0;
-      for (int d = 0; d < s.dim; ++d) dot += double(qf[d]) * h2f(cache[off + d]);
+      for (int d = 0; d < s.dim; ++d) dot += double(qf[d]) * hf[cache[off + d]];
       sc[t] = dot * double(scale);
       mx = std::max(mx, sc[t]);
     }
@@ -356,7 +370,7 @@ void bco_packed_decode(const BcoShape* shape, const uint16_t* q,
       denom += p;
       const long long phys = pages[size_t(b) * s.max_pages + t / kPage];
       const long long off = phys * block_stride + kvh * head_stride + (t % kPage) * slot_stride + kv_offset;
-      for (int d = 0; d < s.dim; ++d) acc[d] += p * h2f(cache[off + d]);
+      for (int d = 0; d < s.dim; ++d) acc[d] += p * hf[cache[off + d]];
     }
     for (int d = 0; d < s.dim; ++d) {
       const float r = denom > 0 ? float(acc[d] / denom) : 0.f;

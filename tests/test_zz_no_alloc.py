@@ -4,11 +4,14 @@ loop whose memory plan forbids per-step allocation): its split partials live in
 a fixed array inside the library instead of caller scratch.
 
 Checked through the C ABI against the existing entry point (bc_decode with
-caller scratch), within the tolerance the decode tests use, on two calls in a
-row with different inputs and split counts, so stale contents of the shared
-array from the first call cannot leak into the second. This file is collected
-last on purpose; it also passes alone in a fresh process (the first call on the
-device performs the array's address look-up).
+caller scratch) and against the CPU oracle, within the tolerance the decode
+tests use, on calls in a row with different inputs and split counts, so stale
+contents of the shared array from one call cannot leak into the next. The
+split counts cover every path the entry point has: 64 and 16 (the global merge
+that bc_decode also takes), 4 (here forced through the array and the global
+merge, where bc_decode merges on chip) and 1 (no merge, the array unused).
+This file is collected last on purpose; it also passes alone in a fresh
+process (the first call on the device performs the array's address look-up).
 """
 import ctypes
 
@@ -17,6 +20,7 @@ import pytest
 import torch
 
 import bc_testutil as U
+import oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -44,18 +48,22 @@ def _reference_call(C, f, t, splits):
 def test_static_scratch_matches_caller_scratch_on_two_calls():
     import bc_capi as C
 
-    f1, t1 = _inputs(101, 4, 6000)
-    f2, t2 = _inputs(202, 3, 2500)
-    out1 = torch.full((4, 32, 128), float("nan"), device="cuda")
-    out2 = torch.full((3, 32, 128), float("nan"), device="cuda")
-    C.decode_static_scratch(C.make_shape(*f1["shape"]), *t1, out1, 64)
-    C.decode_static_scratch(C.make_shape(*f2["shape"]), *t2, out2, 16)
-    ref1 = _reference_call(C, f1, t1, 64)
-    ref2 = _reference_call(C, f2, t2, 16)
+    # (seed, batch, context, splits): consecutive calls share the array
+    calls = [(101, 4, 6000, 64), (202, 3, 2500, 16), (303, 2, 3100, 4), (404, 3, 900, 1)]
+    runs = []
+    for seed, batch, ctx, splits in calls:
+        f, t = _inputs(seed, batch, ctx)
+        out = torch.full((batch, 32, 128), float("nan"), device="cuda")
+        C.decode_static_scratch(C.make_shape(*f["shape"]), *t, out, splits)
+        runs.append((f, t, splits, out))
     torch.cuda.synchronize()
-    for got, ref in ((out1, ref1), (out2, ref2)):
-        assert torch.isfinite(got).all()
-        assert (got - ref).abs().max().item() <= TOL
+    for f, t, splits, out in runs:
+        ref = _reference_call(C, f, t, splits)
+        torch.cuda.synchronize()
+        expected = O.decode(f["shape"], f["q"], f["k"], f["v"], f["pages"], f["lengths"])
+        assert torch.isfinite(out).all()
+        assert (out - ref).abs().max().item() <= TOL, f"splits={splits} vs bc_decode"
+        assert U.max_abs(out.cpu().numpy(), expected) <= TOL, f"splits={splits} vs oracle"
     assert C.last_device_error() == 0
 
 
