@@ -1,41 +1,55 @@
 """Benchmark of the branchcraft B200 hot path.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload tree-cow|tree-oracle|decode|packed|tree-scale|longctx]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--repeats R]
+                    [--impl ours|reference] [--workload W] [--no-extras]
 
-Default workload `tree-cow` (the configuration the headline
-metric is quoted on): one speculative-verification step for 8 requests that
-share a 2040-token paged prefix — `tree_verify` over every request's 7-node
-draft tree, then the copy-on-write commit of every request's accepted path
-(7 shared-page clones + the path rows) — Hq=32, Hkv=8, D=128, FP16 inputs,
-FP32 accumulation and output. `value` is the whole-job algorithmic HBM
-traffic rate (all ranks' bytes / max-over-ranks device time, TB/s);
-`ms_per_step` is the verify+commit step time.
+Headline workload `tree-cow` (the configuration the
+headline metric is quoted on): one speculative-verification step for 8
+requests that share a 2040-token paged prefix — `tree_verify` over every
+request's 7-node draft tree, then the copy-on-write commit of every request's
+accepted path (7 shared-page clones + the path rows) — Hq=32, Hkv=8, D=128,
+FP16 inputs, FP32 accumulation and output. `value` is the whole-job
+algorithmic HBM traffic rate (all ranks' bytes / max-over-ranks device time,
+TB/s); `ms_per_step` is the verify+commit step time.
 
-The other workloads are the remaining BASELINE configurations (one line each,
-for the design notes; the driver runs the default):
+The same run measures every other BASELINE configuration under the key
+`configs` (the driver's BENCH and SCALE runs therefore cover them):
   tree-oracle  config 1: 1 request, 2048-token prefix, 7 nodes, FP16 output
-  decode       config 3: paged split-KV decode, B x context (default 4 x 131072)
+  decode       config 3: paged split-KV decode, 4 x 131072 (batch per rank)
   packed       config 4: vLLM-layout packed decode, B=256, lengths U[512, 8192]
   tree-scale   config 5a: 1024 requests x 63-node trees, 4096-token prefix per 16
-               (strong scaling: the requests are split across ranks)
-  longctx      config 5b: one 1,048,576-token context split across ranks; per-rank
-               FP32 partials all-gathered over NCCL and merged on the device
+               (strong scaling: the 64 prefix groups are split across ranks)
+  longctx      config 5b: one 1,048,576-token context split across ranks; each
+               rank's FP32 partials in one buffer, ONE NCCL all-gather, one
+               on-device merge (strong scaling; decode tokens/s)
+
+Protocol, per workload: W untimed warm-up steps; then R timed regions of K
+steps each, every region bracketed by a barrier and a device synchronisation
+and timed by one pair of CUDA events on the launching stream; the reported
+time is the median region (each region's time the max over ranks). Three
+kinds of region: device steps (inputs resident in HBM; the tiny tree steps
+are replayed from one CUDA graph per rotating input copy, holding exactly the
+C-ABI calls a step makes), the dominant kernel alone (K launches back to back
+through the C ABI: its average launch duration, for the roofline), and end to
+end (each step's inputs copied from pinned host memory and its result copied
+back, through the C ABI). Workloads whose one-step working set is smaller than
+L2 (tree-cow, tree-oracle) rotate over enough independent copies of it (K/V
+pool, step inputs, output) to exceed twice the L2 size, so every step reads
+cold data; the others stream more than L2 per step.
 
 One process per GPU (torchrun for N > 1). Request-sharded workloads run every
-rank on its own batch (weak scaling, no data-path collective). Workloads whose
-one-step working set is smaller than L2 (tree-cow, tree-oracle) rotate over
-enough independent copies of it (K/V pool, step inputs, output) to exceed
-twice the L2 size, so every step reads cold data; the others stream more than
-L2 per step.
+rank on its own batch (weak scaling, no data-path collective).
 
 `--impl reference` times the reference's own CPU implementation on rank 0 (its
 CPU oracle, compiled unmodified from src/main.cu into oracle/_ref/libbcref.so,
-one request per host thread), on the same inputs and in the same unit.
+one request per host thread), on the same inputs and in the same unit, and
+beside it the reference's own GPU kernels (its src/*.cu built for sm_100a)
+on the configurations they can run.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -53,14 +67,14 @@ sys.path.insert(0, str(ROOT / "branchcraft-cuda_b200"))
 
 METRIC = "tree_verify µs & HBM TB/s per B200; decode tokens/s at 1/2/4/8 GPUs"
 PEAKS = ROOT / "MEASURED_PEAKS.json"
-FLUSH_BYTES = 256 << 20
 SCALE = 1.0 / math.sqrt(128.0)
+L2_BYTES = 126 << 20
 
 # DRAM bytes per launch of each workload's dominant kernel (dram__bytes_read.sum
 # + dram__bytes_write.sum) from one ncu capture of `python bench.py --workload W
-# --steps 1..3 --warmup 3 --no-cpu-baseline` on a B200. `packed` was captured at
-# --batch 64 (266,106 tokens) and is scaled by tokens to the 256-request batch
-# (1,142,306 tokens): its traffic is a per-token stream.
+# --steps 1..3 --warmup 3 --no-cpu-baseline --no-extras` on a B200. `packed`
+# was captured at --batch 64 (266,106 tokens) and is scaled by tokens to the
+# 256-request batch (1,142,306 tokens): its traffic is a per-token stream.
 NCU_TRAFFIC = {
     "tree-cow": 9176320,
     "tree-scale": 1880985000 + 514538240,
@@ -86,6 +100,7 @@ class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, device_index: int):
         self.samples = []
@@ -113,18 +128,27 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
 
+    @classmethod
+    def _reasons(cls, rows):
+        out = set()
+        for p in rows:
+            for name, val in zip(cls.NAMES, p[5:9]):
+                if val.lower().startswith("active"):
+                    out.add(name)
+        return sorted(out)
+
     def window(self, t0, t1):
         inside = [p for t, p in self.samples if t0 <= t <= t1]
-        bracketing = False
+        bracket = []
         if len(inside) < 2 and self.samples:
-            # A region shorter than two sample periods: add the last sample
-            # before it and the first after it, which bound its clocks.
+            # A region shorter than two sample periods: the last sample before
+            # it and the first after it bound its clocks.
             before = [s for s in self.samples if s[0] < t0]
             after = [s for s in self.samples if s[0] > t1]
-            inside = (([max(before, key=lambda s: s[0])[1]] if before else []) + inside +
-                      ([min(after, key=lambda s: s[0])[1]] if after else []))
-            bracketing = True
-        if not inside:
+            bracket = (([max(before, key=lambda s: s[0])[1]] if before else []) +
+                       ([min(after, key=lambda s: s[0])[1]] if after else []))
+        rows = inside + bracket
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
 
         def num(x):
@@ -133,18 +157,16 @@ class ClockSampler:
             except ValueError:
                 return None
 
-        sm = [num(p[1]) for p in inside if num(p[1]) is not None]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for p in inside:
-            for name, val in zip(names, p[5:9]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
+        sm = [num(p[1]) for p in rows if num(p[1]) is not None]
         out = {"sm_mhz": statistics.median(sm) if sm else None,
-               "sm_max_mhz": num(inside[0][2]), "reasons": sorted(reasons),
-               "samples": len(inside)}
-        if bracketing:
-            out["bracketing"] = True  # samples just before and after the region
+               "sm_max_mhz": num(rows[0][2]), "samples": len(rows)}
+        # Throttle reasons come from the samples inside the region when there
+        # are any; the bracketing samples' own reasons are listed apart.
+        out["reasons"] = self._reasons(inside if inside else bracket)
+        if bracket:
+            out["bracketing"] = True
+            out["samples_inside"] = len(inside)
+            out["reasons_bracketing"] = self._reasons(bracket)
         return out
 
 
@@ -166,19 +188,32 @@ def half_bits(torch, t):
 
 
 def oracle_module():
+    """The CPU oracle (test infrastructure): loaded only by the CPU-baseline
+    leg and the reference arm."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as O
 
     return O
 
 
+def region(torch, fn, steps, stream):
+    """Device time (ms) of `steps` calls of fn between one pair of CUDA events
+    recorded on `stream`."""
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        fn()
+    b.record(stream)
+    b.synchronize()
+    return a.elapsed_time(b)
+
+
 class CudaRt:
     """The few CUDA runtime calls the pipelined end-to-end loop makes, called
     directly (torch's stream/event/copy wrappers cost several microseconds of
-    host time each, which would make a 30 µs step host-bound)."""
+    host time each, which would make a 20 µs step host-bound)."""
 
     def __init__(self):
-        import ctypes
         import glob
 
         import torch  # noqa: F401  (loads the runtime torch uses)
@@ -196,15 +231,13 @@ class CudaRt:
         self.rt.cudaEventCreateWithFlags.argtypes = [ctypes.POINTER(vp), ctypes.c_uint]
         self.rt.cudaEventRecord.argtypes = [vp, vp]
         self.rt.cudaStreamWaitEvent.argtypes = [vp, vp, ctypes.c_uint]
-        self.rt.cudaEventDestroy.argtypes = [vp]
-        self.ctypes = ctypes
 
     def event(self):
-        e = self.ctypes.c_void_p()
-        assert self.rt.cudaEventCreateWithFlags(self.ctypes.byref(e), 2) == 0  # no timing
+        e = ctypes.c_void_p()
+        assert self.rt.cudaEventCreateWithFlags(ctypes.byref(e), 2) == 0  # no timing
         return e
 
-    def copy(self, dst, src, nbytes, kind, stream):  # kind 1: H2D, 2: D2H
+    def copy(self, dst, src, nbytes, kind, stream):  # kind 1: H2D, 2: D2H, 3: D2D
         assert self.rt.cudaMemcpyAsync(dst, src, nbytes, kind, stream) == 0
 
     def record(self, ev, stream):
@@ -220,14 +253,12 @@ class PackedInputs:
     host-to-device copy; `dev[name]` are typed views into the device buffer."""
 
     def __init__(self, torch, arrays, device):
-        import torch as _t
-
         offs, off = {}, 0
         tens = {}
         for n, a in arrays.items():
-            t = a if isinstance(a, _t.Tensor) else (
-                _t.from_numpy(np.ascontiguousarray(a).view(np.int16).copy()).view(_t.float16)
-                if np.asarray(a).dtype == np.uint16 else _t.from_numpy(np.ascontiguousarray(a).copy()))
+            t = a if isinstance(a, torch.Tensor) else (
+                torch.from_numpy(np.ascontiguousarray(a).view(np.int16).copy()).view(torch.float16)
+                if np.asarray(a).dtype == np.uint16 else torch.from_numpy(np.ascontiguousarray(a).copy()))
             t = t.contiguous().cpu()
             tens[n] = t
             offs[n] = off
@@ -242,38 +273,43 @@ class PackedInputs:
                     .view(t.dtype).view(t.shape) for n, t in tens.items()}
         self.payload = sum(t.numel() * t.element_size() for t in tens.values())
 
-    def upload(self):
-        self.buf.copy_(self.host, non_blocking=True)
-
-
-class Events:
-    """Pairs of CUDA events recorded on a stream; `ms()` their durations."""
-
-    def __init__(self, torch, n):
-        self.ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                   for _ in range(n)]
-
-    def ms(self):
-        return [a.elapsed_time(b) for a, b in self.ev]
-
 
 # --------------------------------------------------------------- workloads
-# Each workload: setup(), device_step(i, kev), e2e_step(), and facts for the
-# JSON line. `kev` is a pair of events bracketing the dominant kernel.
+# Each workload: device_step() (one step, inputs resident), kernel_step() (the
+# dominant kernel alone), e2e_region(K) or e2e_step() (host copies included),
+# and the facts of its JSON entry.
+class Workload:
+    flush = False
+    higher_is_better = True
+    scaling = "weak"
+    kernel_launches = 1  # launches per kernel_step
+    graphed = False
 
-L2_BYTES = 126 << 20
+    def prepare(self):
+        """After warm-up, before timing (e.g. capture CUDA graphs)."""
+
+    def release(self):
+        """Drop device memory before the next workload."""
+        for n in list(vars(self)):
+            if n not in ("torch", "C", "device"):
+                delattr(self, n)
+
+    def l2_note(self):
+        return "inputs larger than L2 (no flush)"
+
+    def reference_step(self, pool):
+        return None
 
 
-class TreeCow:
+class TreeCow(Workload):
     """Config 2. The working set of one step (K/V pool, draft inputs, output)
     is far below L2, so the bench rotates over `copies` independent copies of
     all of it, more than twice the L2 size in total: each step touches data
     last used `copies` steps earlier (cold in L2) and no flush kernel runs
-    between steps."""
+    between steps. Device steps are replayed from one CUDA graph per copy,
+    each holding the step's two C-ABI calls (bc_tree_verify, bc_commit_batch)."""
 
     name = "tree-cow"
-    flush = False
-    higher_is_better = True
     unit = "TB/s"
 
     def __init__(self, torch, C, device, rank, world, **_):
@@ -317,24 +353,22 @@ class TreeCow:
         self.out_hosts = [torch.empty(self.out_shape, dtype=self.out_dtype).pin_memory()
                           for _ in range(self.copies)]
         self.rot = 0
+        self._argv = {}
 
     def _next(self):
         c = self.rot
         self.rot = (self.rot + 1) % self.copies
         return c
 
-    def _args(self, c):
-        """The C-ABI argument tuples of copy c (built once: the bench loop
-        then costs one foreign call per entry point)."""
-        import ctypes
-
-        if not hasattr(self, "_argv"):
-            self._argv = {}
-        if c not in self._argv:
+    def _args(self, c, stream):
+        """The C-ABI argument tuples of copy c on `stream` (built once: a
+        step then costs one foreign call per entry point)."""
+        key = (c, stream.cuda_stream)
+        if key not in self._argv:
             d, C = self.ios[c].dev, self.C
             ck, cv = self.caches[c]
             P = C._ptr
-            st = C._stream()
+            st = ctypes.c_void_p(stream.cuda_stream)
             tv = (ctypes.byref(self.shape), P(d["draft_q"]), P(ck), P(cv), P(d["pages"]),
                   P(d["lengths"]), P(d["draft_k"]), P(d["draft_v"]), P(d["parent"]),
                   P(self.outs[c]), self.nodes, st)
@@ -346,35 +380,53 @@ class TreeCow:
                       P(d["e_page"]), P(d["e_slot"]), int(d["e_node"].numel()), st)
             fn = (C.lib().bc_tree_verify_f16 if self.out_dtype == self.torch.float16
                   else C.lib().bc_tree_verify)
-            self._argv[c] = (fn, tv, cb)
-        return self._argv[c]
+            self._argv[key] = (fn, tv, cb)
+        return self._argv[key]
 
-    def launch(self, c, kev=None):
-        fn, tv, cb = self._args(c)
-        if kev:
-            kev[0].record()
+    def launch(self, c, stream=None, verify_only=False):
+        fn, tv, cb = self._args(c, stream or self.torch.cuda.current_stream())
         rc = fn(*tv)
-        if kev:
-            kev[1].record()
-        if cb is not None and rc == 0:
+        if cb is not None and rc == 0 and not verify_only:
             rc = self.C.lib().bc_commit_batch(*cb)
         if rc != 0:
             raise self.C.BranchcraftError(f"bench step failed with cudaError {rc}")
 
-    def device_step(self, kev=None):
-        self.launch(self._next(), kev)
+    def prepare(self):
+        """One CUDA graph per rotating copy, captured from the step's C-ABI
+        calls (the library's per-device caches are warm by now)."""
+        torch = self.torch
+        self.graphs = []
+        cap = torch.cuda.Stream()
+        for c in range(self.copies):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                self.launch(c, cap)
+            self.graphs.append(g)
+        torch.cuda.synchronize()
+        self.graphed = True
+
+    def device_step(self):
+        c = self._next()
+        if self.graphed:
+            self.graphs[c].replay()
+        else:
+            self.launch(c)
+
+    def kernel_step(self):
+        self.launch(self._next(), verify_only=True)
 
     def e2e_step(self):
         c = self._next()
-        self.ios[c].upload()
+        io = self.ios[c]
+        io.buf.copy_(io.host, non_blocking=True)
         self.launch(c)
         self.out_hosts[c].copy_(self.outs[c], non_blocking=True)
 
-    def e2e_run(self, steps, flush):
+    def e2e_region(self, steps):
         """`steps` end-to-end steps as a serving loop runs them: step i's
         inputs go host-to-device on one copy stream, its result device-to-host
-        on another, so copies of neighbouring steps overlap the compute.
-        Returns the device time of the whole run (ms)."""
+        on another, so copies of neighbouring steps overlap the compute; the
+        compute is the step's two C-ABI calls. Returns the device time (ms)."""
         torch = self.torch
         if not hasattr(self, "h2d"):
             self.h2d, self.d2h = torch.cuda.Stream(), torch.cuda.Stream()
@@ -385,12 +437,13 @@ class TreeCow:
             self.ev_down = [self.rt.event() for _ in range(n)]
         rt, n = self.rt, self.copies
         main = torch.cuda.current_stream()
-        ms, hs, ds = (self.C.ctypes.c_void_p(x.cuda_stream) for x in (main, self.h2d, self.d2h))
+        ms, hs, ds = (ctypes.c_void_p(x.cuda_stream) for x in (main, self.h2d, self.d2h))
         out_bytes = int(np.prod(self.out_shape)) * (4 if self.out_dtype == torch.float32 else 2)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record(main)
         self.h2d.wait_stream(main)
         self.d2h.wait_stream(main)
+        self.rot = 0
         for i in range(steps):
             c = self._next()
             io = self.ios[c]
@@ -401,7 +454,7 @@ class TreeCow:
             rt.wait(ms, self.ev_up[c])
             if i >= n:
                 rt.wait(ms, self.ev_down[c])  # copy c's previous result has been read back
-            self.launch(c)
+            self.launch(c, main)
             rt.record(self.ev_done[c], ms)
             rt.wait(ds, self.ev_done[c])
             rt.copy(self.out_hosts[c].data_ptr(), self.outs[c].data_ptr(), out_bytes, 2, ds)
@@ -461,7 +514,7 @@ class TreeCow:
 
     def reference_step(self, pool):
         """The reference's cpu_tree_reference per request (one per thread) +
-        the sequential COW commits; returns (seconds, bytes)."""
+        the sequential COW commits; returns (seconds, bytes, units)."""
         O = oracle_module()
         from cow_oracle import CowOracle
 
@@ -487,15 +540,16 @@ class TreeCow:
 
 class TreeOracle(TreeCow):
     """one request, 2048-token prefix in a seeded permutation
-    of a 256-page pool, parents [-1,0,0,1,1,2,2], FP16 output."""
+    of a 256-page pool, parents [-1,0,0,1,1,2,2], FP16 output; one CUDA graph
+    (the bc_tree_verify_f16 call) per rotating copy."""
 
     name = "tree-oracle"
 
     def __init__(self, torch, C, device, rank, world, **_):
-        self.torch, self.C, self.device = torch, C, device
-        rng = np.random.default_rng(2048 + rank)
         from bc_workloads import rand_half
 
+        self.torch, self.C, self.device = torch, C, device
+        rng = np.random.default_rng(2048 + rank)
         P, prefix, N = 256, 2048, 7
         self.N = self.nodes = N
         self.prefix = prefix
@@ -600,6 +654,10 @@ class TreeHbm(TreeCow):
         self.out_hosts = [torch.empty(self.out_shape, dtype=self.out_dtype).pin_memory()
                           for _ in range(self.copies)]
         self.rot = 0
+        self._argv = {}
+
+    def prepare(self):
+        """Half-millisecond steps: direct calls, no graph."""
 
     def config(self):
         return {"workload": f"tree_verify, {self.batch} requests x {self.prefix}-token private "
@@ -630,13 +688,12 @@ class TreeHbm(TreeCow):
         return None
 
 
-class Decode:
+class Decode(Workload):
     """paged split-KV decode of `batch` one-token requests
-    over `context` tokens each (pages in a seeded random permutation)."""
+    over `context` tokens each (pages in a seeded random permutation); every
+    rank its own batch (weak scaling)."""
 
     name = "decode"
-    flush = False
-    higher_is_better = True
     unit = "tokens/s"
 
     def __init__(self, torch, C, device, rank, world, batch=0, context=0, splits=0, **_):
@@ -662,18 +719,18 @@ class Decode:
         self.out = torch.empty(batch, 32, 128, device=device)
         self.out_host = torch.empty(self.out.shape).pin_memory()
         self.launches = 1 + (self.splits > 8)
+        self.kernel_launches = self.launches
         self.kernel_bytes = batch * context * 4096 + rows * 128 * 2 + rows * 128 * 4
         self.step_bytes = self.kernel_bytes
-        self.kernel = "attn_kernel (paged decode) + merge"
+        self.kernel = ("attn_kernel (paged decode)" +
+                       (" + merge_kernel (the events bracket both)" if self.splits > 8 else ""))
         self.bound = "hbm"
 
-    def device_step(self, kev=None):
-        if kev:
-            kev[0].record()
+    def device_step(self):
         self.C.decode(self.shape, self.q, self.k, self.v, self.pages, self.lengths, self.out,
                       self.pa, self.pml, self.splits)
-        if kev:
-            kev[1].record()
+
+    kernel_step = device_step
 
     def e2e_step(self):
         self.q.copy_(self.q_host, non_blocking=True)
@@ -724,7 +781,8 @@ class Decode:
 
 
 class Packed(Decode):
-    """vLLM-layout packed decode, B=256, lengths U[512, 8192]."""
+    """BASELINE config 4: vLLM-layout packed decode, B=256, lengths U[512, 8192];
+    every rank its own batch (weak scaling)."""
 
     name = "packed"
 
@@ -749,25 +807,24 @@ class Packed(Decode):
         self.lengths = torch.from_numpy(lens).to(device)
         self.lens = lens
         self.batch = batch
+        self.nb, self.mp = nb, mp
         self.shape = C.make_shape(batch, 32, 8, 128, mp, nb)
         self.q_host = torch.randn(batch, 32, 128, dtype=torch.float16).pin_memory()
         self.q = self.q_host.to(device)
         self.out = torch.empty(batch, 32, 128, device=device, dtype=torch.float16)
         self.out_host = torch.empty(self.out.shape, dtype=torch.float16).pin_memory()
-        self.launches = 1
+        self.launches = self.kernel_launches = 1
         rows = batch * 32
         self.kernel_bytes = int(lens.sum()) * 4096 + rows * 128 * 2 * 2 + batch * mp * 4
         self.step_bytes = self.kernel_bytes
         self.kernel = "attn_kernel (packed decode)"
         self.bound = "hbm"
 
-    def device_step(self, kev=None):
-        if kev:
-            kev[0].record()
+    def device_step(self):
         self.C.packed_decode_kv(self.shape, self.q, self.cache, self.pages, self.lengths,
                                 self.out, 2 * 16 * 8 * 128, 128, 8 * 128, 16 * 8 * 128, SCALE, 0)
-        if kev:
-            kev[1].record()
+
+    kernel_step = device_step
 
     def io_bytes(self):
         return self.q_host.numel() * 2, self.out_host.numel() * 2
@@ -800,15 +857,15 @@ class Packed(Decode):
         return None
 
 
-class TreeScale:
-    """BASELINE config 5a: 1024 requests (split across ranks), each a 63-node
-    full binary tree over a 4096-token prefix shared by groups of 16 requests;
-    FP16 output. Tensor-bound: value = whole-job TFLOP/s."""
+class TreeScale(Workload):
+    """BASELINE config 5a: 1024 requests (whole 16-request prefix groups split
+    across ranks), each a 63-node full binary tree over a 4096-token prefix
+    shared by its group; FP16 output. Tensor-bound: value = whole-job
+    TFLOP/s."""
 
     name = "tree-scale"
-    flush = False
-    higher_is_better = True
     unit = "TFLOP/s"
+    scaling = "strong"
 
     def __init__(self, torch, C, device, rank, world, total=1024, group=16, prefix=4096,
                  nodes=63, **_):
@@ -840,6 +897,7 @@ class TreeScale:
         self.flops = 32 * 4 * 128 * B * (nodes * prefix + depth_sum)
         self.unique_bytes = (ngroups * prefix * 4096 + B * nodes * 8 * 128 * 4
                              + B * nodes * 32 * 128 * 4 + B * npg * 4)
+        self.kernel_bytes = self.unique_bytes
         self.launches = 1
         self.kernel = "tree_mma_kernel (tree_verify, FP16 out)"
         self.bound = "tensor"
@@ -849,13 +907,11 @@ class TreeScale:
                      for n in ("dq", "dk", "dv", "parent", "pages", "lengths")}
         self.out_host = torch.empty(self.out.shape, dtype=torch.float16).pin_memory()
 
-    def device_step(self, kev=None):
-        if kev:
-            kev[0].record()
+    def device_step(self):
         self.C.tree_verify(self.shape, self.dq, self.k, self.v, self.pages, self.lengths,
                            self.dk, self.dv, self.parent, self.out, self.N)
-        if kev:
-            kev[1].record()
+
+    kernel_step = device_step
 
     def e2e_step(self):
         for n, t in self.host.items():
@@ -874,7 +930,8 @@ class TreeScale:
         return {"workload": "BASELINE config 5a: tree_verify, 1024 requests x 63-node full "
                             "binary trees, 4096-token prefix shared per 16 requests, FP16 out",
                 "requests_per_gpu": self.B, "flops_per_step": self.flops,
-                "unique_bytes_per_step": self.unique_bytes, "parallelism": "request-sharded"}
+                "unique_bytes_per_step": self.unique_bytes,
+                "parallelism": "request-sharded (whole prefix groups)"}
 
     def cpu_baseline(self):
         O = oracle_module()
@@ -894,24 +951,21 @@ class TreeScale:
                 "cores": O.max_threads(), "kind": "port",
                 "sample": "1 request (63 nodes x 4096-token prefix)", "seconds": round(dt, 4)}
 
-    def reference_step(self, pool):
-        return None
 
-
-class LongCtx:
+class LongCtx(Workload):
     """BASELINE config 5b: one request of 1,048,576 tokens; rank r holds a
     contiguous 1/world shard of its pages and reduces it to FP32 partials
-    (m, l, acc) — `splits` of them per q-head, unmerged, when splits > 8 —
-    which are all-gathered over NCCL and merged on the device in one launch.
-    value = tokens/s (one decoded token per job step); strong scaling."""
+    (m, l, acc) — `splits` of them per q-head, unmerged, when splits > 8 — in
+    ONE buffer, which a single NCCL all-gather brings to every rank, where one
+    launch merges all of them (bc_merge_gathered). value = tokens/s (one
+    decoded token per job step); strong scaling."""
 
     name = "longctx"
-    flush = False
-    higher_is_better = True
     unit = "tokens/s"
+    scaling = "strong"
 
     def __init__(self, torch, C, device, rank, world, total=1 << 20, splits=0, **_):
-        from bc_dist import shard_pages
+        from bc_dist import block_floats, block_views, shard_pages
 
         self.torch, self.C, self.device, self.world = torch, C, device, world
         npg_total = total // 16
@@ -934,36 +988,36 @@ class LongCtx:
         self.q_host = torch.randn(1, 32, 128, dtype=torch.float16, generator=gq).pin_memory()
         self.q = self.q_host.to(device)
         self.out_host = torch.empty(1, 32, 128).pin_memory()
-        self.pml = torch.empty(self.S, 32, 2, device=device)
-        self.pa = torch.empty(self.S, 32, 128, device=device)
-        self.g_ml = torch.empty(world, self.S, 32, 2, device=device)
-        self.g_a = torch.empty(world, self.S, 32, 128, device=device)
+        self.buf = torch.empty(block_floats(self.S, 32, 128), device=device)
+        self.pml, self.pa = block_views(self.buf, self.S, 32, 128)
+        self.gathered = torch.empty(world, self.buf.numel(), device=device)
         self.out = torch.empty(32, 128, device=device)
         self.total = total
         self.kernel_bytes = npg * 16 * 4096 + 32 * 128 * 2 + self.S * 32 * 130 * 4
         self.step_bytes = self.kernel_bytes
-        self.launches = 2  # rank-local partial decode + merge of every partial
+        self.launches = 2  # rank-local partial decode + merge of every rank's partials
         self.kernel = "attn_kernel (paged decode partial)"
         self.bound = "hbm"
+        self.group = None
+        if world > 1:
+            from bc_dist import exchange_group
 
-    def device_step(self, kev=None):
-        C = self.C
-        if kev:
-            kev[0].record()
-        C.paged_decode_partial(self.shape, self.q, self.k, self.v, self.pages, self.lengths,
-                               self.pml, self.pa, self.splits)
-        if kev:
-            kev[1].record()
+            self.group = exchange_group()
+
+    def kernel_step(self):
+        self.C.paged_decode_partial(self.shape, self.q, self.k, self.v, self.pages, self.lengths,
+                                    self.pml, self.pa, self.splits)
+
+    def device_step(self):
+        self.kernel_step()
         if self.world > 1:
             import torch.distributed as dist
 
-            dist.all_gather_into_tensor(self.g_ml, self.pml)
-            dist.all_gather_into_tensor(self.g_a, self.pa)
-            g_ml, g_a = self.g_ml, self.g_a
+            dist.all_gather_into_tensor(self.gathered, self.buf, group=self.group)
+            g = self.gathered
         else:
-            g_ml, g_a = self.pml.unsqueeze(0), self.pa.unsqueeze(0)
-        n = self.world * self.S
-        C.merge_partials(g_ml.view(n, 32, 2), g_a.view(n, 32, 128), self.out)
+            g = self.buf.view(1, -1)
+        self.C.merge_gathered(g, self.world, self.S, 32, 128, self.out)
 
     def e2e_step(self):
         self.q.copy_(self.q_host, non_blocking=True)
@@ -978,10 +1032,18 @@ class LongCtx:
 
     def config(self):
         return {"workload": "BASELINE config 5b: one request, 1,048,576-token context split "
-                            "across ranks, FP32 partials all-gathered (NCCL) and merged",
+                            "across ranks, FP32 partials all-gathered (one NCCL all-gather of "
+                            "one buffer per rank) and merged on the device",
                 "tokens_per_gpu": int(self.lengths[0]), "splits_per_gpu": self.splits,
                 "parallelism": f"context-split x{self.world}",
-                "collective_bytes_per_rank": self.S * 32 * (128 + 2) * 4}
+                "collective_bytes_per_rank": self.buf.numel() * 4}
+
+    def release(self):
+        if getattr(self, "group", None) is not None:
+            import torch.distributed as dist
+
+            dist.destroy_process_group(self.group)
+        super().release()
 
     def cpu_baseline(self, tokens=65536):
         O = oracle_module()
@@ -998,14 +1060,119 @@ class LongCtx:
                 "sample": f"a {tokens}-token slice, scaled linearly to {self.total} tokens",
                 "seconds": round(dt, 4)}
 
-    def reference_step(self, pool):
-        return None
-
 
 WORKLOADS = {w.name: w for w in (TreeCow, TreeOracle, TreeHbm, Decode, Packed, TreeScale, LongCtx)}
+# Measured after the headline in the default run, each under line["configs"].
+EXTRAS = ("tree-oracle", "decode", "packed", "tree-scale", "longctx")
 
 
 # --------------------------------------------------------------- our arm
+class Harness:
+    """Process-group plumbing and the timed-region protocol shared by every
+    workload of one run."""
+
+    def __init__(self, torch, world, rank, device, repeats):
+        self.torch, self.world, self.rank, self.device = torch, world, rank, device
+        self.repeats = repeats
+        self.hbm_peak, self.tensor_peak, self.peak_kind = load_peaks()
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max_over_ranks(self, values):
+        if self.world == 1:
+            return list(values)
+        import torch.distributed as dist
+
+        t = self.torch.tensor(values, device=self.device, dtype=self.torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(x) for x in t]
+
+    def measure(self, wl, steps, warmup, sampler, with_cpu):
+        torch, C = self.torch, wl.C
+        stream = torch.cuda.current_stream()
+        for _ in range(warmup):
+            wl.device_step()
+            wl.kernel_step()
+            wl.e2e_step()
+        torch.cuda.synchronize()
+        if C.last_device_error() != 0:
+            raise SystemExit(f"device error word set during {wl.name} warm-up")
+        wl.prepare()
+        for _ in range(2):  # the captured form, once more untimed
+            wl.device_step()
+        torch.cuda.synchronize()
+        R = self.repeats
+        dev, kern, e2e = [], [], []
+        t0 = time.time()
+        for _ in range(R):
+            self.barrier()
+            dev.append(region(torch, wl.device_step, steps, stream))
+        for _ in range(R):
+            self.barrier()
+            kern.append(region(torch, wl.kernel_step, steps, stream))
+        for _ in range(R):
+            self.barrier()
+            if hasattr(wl, "e2e_region"):
+                e2e.append(wl.e2e_region(steps))
+            else:
+                e2e.append(region(torch, wl.e2e_step, steps, stream))
+        self.barrier()
+        t1 = time.time()
+        err = C.last_device_error()
+        allv = self.max_over_ranks(dev + kern + e2e + [float(err)])
+        dev, kern, e2e, err = allv[:R], allv[R:2 * R], allv[2 * R:3 * R], int(allv[-1])
+        dev_ms, kern_ms, e2e_ms = (statistics.median(x) for x in (dev, kern, e2e))
+        world = self.world
+        value = wl.value(steps * world, dev_ms * 1e-3)
+        e2e_value = wl.value(steps * world, e2e_ms * 1e-3)
+        kern_us = kern_ms * 1e3 / steps
+        if wl.bound == "tensor":
+            achieved = wl.flops / (kern_us * 1e-6) / 1e12
+            roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": self.tensor_peak,
+                    "unit": "TFLOP/s", "frac": round(achieved / self.tensor_peak, 4),
+                    "peak_source": f"{self.peak_kind} bf16_tflops (FP16 = BF16 rate)"}
+        else:
+            achieved = wl.kernel_bytes / (kern_us * 1e-6) / 1e9
+            roof = {"bound": "hbm", "achieved": round(achieved, 2), "peak": self.hbm_peak,
+                    "unit": "GB/s", "frac": round(achieved / self.hbm_peak, 4),
+                    "peak_source": f"{self.peak_kind} hbm_gbs"}
+        roof["kernel"] = wl.kernel
+        roof["kernel_us"] = round(kern_us, 3)
+        roof["timing"] = (f"median of {R} regions of {steps} back-to-back launches through the "
+                          "C ABI, one event pair per region")
+        roof["traffic"] = NCU_TRAFFIC.get(wl.name)
+        h2d, d2h = wl.io_bytes()
+        cfg = wl.config()
+        cfg["l2"] = wl.l2_note()
+        cfg.setdefault("parallelism", f"request-sharded x{world}")
+        out = {
+            "value": round(value, 6), "unit": wl.unit, "higher_is_better": wl.higher_is_better,
+            "scaling": wl.scaling, "ms_per_step": round(dev_ms / steps, 6),
+            "ms_per_step_regions": [round(x / steps, 6) for x in dev],
+            "step_form": ("one CUDA graph replay per step (the step's C-ABI calls, captured "
+                          "per rotating input copy)" if wl.graphed else
+                          "the step's C-ABI calls issued directly"),
+            "config": cfg,
+            "e2e": {"value": round(e2e_value, 6), "unit": wl.unit, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / steps, 6),
+                    "mode": ("pipelined: next step's H2D and previous step's D2H overlap the "
+                             "compute" if hasattr(wl, "e2e_region") else
+                             "sequential: H2D, compute, D2H per step")},
+            "gpu_launches": R * steps * (2 * wl.launches + wl.kernel_launches),
+            "roofline": roof, "clocks": sampler.window(t0, t1), "device_error_word": err,
+        }
+        if with_cpu:
+            cb = wl.cpu_baseline()
+            cb["value"] = float(f"{cb['value']:.6g}")
+            out["cpu_baseline"] = cb
+        return out
+
+
 def run_ours(args):
     import torch
 
@@ -1024,132 +1191,39 @@ def run_ours(args):
 
     import bc_capi as C
 
-    hbm_peak, tensor_peak, peak_kind = load_peaks()
-    wl = WORKLOADS[args.workload](torch, C, device, rank, world, batch=args.batch,
-                                  context=args.context, splits=args.splits)
-    flush = torch.empty(FLUSH_BYTES // 4, device=device) if wl.flush else None
-    stream = torch.cuda.current_stream()
-
-    def barrier():
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    for _ in range(args.warmup):
-        if flush is not None:
-            flush.fill_(1.0)
-        wl.device_step()
-        wl.e2e_step()
-    torch.cuda.synchronize()
-    if C.last_device_error() != 0:
-        raise SystemExit("device error word set during warm-up")
-
+    h = Harness(torch, world, rank, device, args.repeats)
     sampler = ClockSampler(device.index)
     time.sleep(0.3)
-    # Timed region 1: the K steps. Without a flush between steps, one pair of
-    # events on the launching stream brackets all of them (host gaps count;
-    # consecutive steps' kernels are programmatic dependents of one another and
-    # an event in between would serialise them); with a flush, a pair per step.
-    barrier()
-    t0 = time.time()
-    if flush is None:
-        steps = Events(torch, 1)
-        steps.ev[0][0].record(stream)
-        for i in range(args.steps):
-            wl.device_step()
-        steps.ev[0][1].record(stream)
-    else:
-        steps = Events(torch, args.steps)
-        for i in range(args.steps):
-            flush.fill_(1.0)
-            steps.ev[i][0].record(stream)
-            wl.device_step()
-            steps.ev[i][1].record(stream)
-    barrier()
-    t1 = time.time()
-    # Timed region 2: the same steps with the dominant kernel bracketed by its
-    # own events (its duration for the roofline).
-    kern = Events(torch, args.steps)
-    barrier()
-    for i in range(args.steps):
-        if flush is not None:
-            flush.fill_(1.0)
-        wl.device_step(kern.ev[i])
-    barrier()
-    # Timed region 3: end to end through the public API, host buffers in and out.
-    barrier()
-    if hasattr(wl, "e2e_run"):
-        total_e2e = wl.e2e_run(args.steps, flush)
-        e2e_mode = "pipelined: next step's H2D and previous step's D2H overlap the compute"
-    else:
-        e2e = Events(torch, args.steps)
-        for i in range(args.steps):
-            if flush is not None:
-                flush.fill_(1.0)
-            e2e.ev[i][0].record(stream)
-            wl.e2e_step()
-            e2e.ev[i][1].record(stream)
-        torch.cuda.synchronize()
-        total_e2e = sum(e2e.ms())
-        e2e_mode = "sequential: H2D, compute, D2H per step"
-    barrier()
+    with_cpu = world == 1 and not args.no_cpu_baseline
+    kw = dict(batch=args.batch, context=args.context, splits=args.splits)
+    wl = WORKLOADS[args.workload](torch, C, device, rank, world, **kw)
+    head = h.measure(wl, args.steps, args.warmup, sampler, with_cpu and rank == 0)
+    if args.batch or args.context or args.splits or args.traffic is not None:
+        head["roofline"]["traffic"] = args.traffic
+    wl.release()
+    del wl
+    torch.cuda.empty_cache()
+    extras = {}
+    if args.workload == "tree-cow" and not args.no_extras:
+        for name in EXTRAS:
+            w = WORKLOADS[name](torch, C, device, rank, world)
+            extras[name] = h.measure(w, args.steps, args.warmup, sampler, with_cpu and rank == 0)
+            w.release()
+            del w
+            torch.cuda.empty_cache()
     sampler.stop()
-    err = C.last_device_error()
-    step_ms, kern_ms = steps.ms(), kern.ms()
-    total_ms = sum(step_ms)
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([total_ms, total_e2e, float(err)], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, total_e2e, err = float(t[0]), float(t[1]), int(t[2])
-
-    value = wl.value(args.steps * world, total_ms * 1e-3)
-    e2e_value = wl.value(args.steps * world, total_e2e * 1e-3)
-    kern_us = statistics.mean(kern_ms) * 1e3
-    if wl.bound == "tensor":
-        achieved = wl.flops / (kern_us * 1e-6) / 1e12
-        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": tensor_peak,
-                "unit": "TFLOP/s", "frac": round(achieved / tensor_peak, 4),
-                "peak_source": f"{peak_kind} bf16_tflops (FP16 = BF16 rate)"}
-    else:
-        achieved = wl.kernel_bytes / (kern_us * 1e-6) / 1e9
-        roof = {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak,
-                "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                "peak_source": f"{peak_kind} hbm_gbs"}
-    roof["kernel"] = wl.kernel
-    roof["kernel_us"] = round(kern_us, 3)
-    default_shape = not (args.batch or args.context or args.splits)
-    roof["traffic"] = (args.traffic if args.traffic is not None or not default_shape
-                       else NCU_TRAFFIC.get(wl.name))
-    h2d, d2h = wl.io_bytes()
-    cfg = wl.config()
-    cfg["l2"] = (wl.l2_note() if hasattr(wl, "l2_note") else
-                 "flushed between timed steps (256 MiB device write, outside the step events)"
-                 if wl.flush else "inputs larger than L2 (no flush)")
-    cfg.setdefault("parallelism", f"request-sharded x{world}")
     if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 6), "unit": wl.unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(total_ms / args.steps, 6),
-            "host_ms_per_step": round((t1 - t0) * 1e3 / args.steps, 6),
-            "higher_is_better": wl.higher_is_better,
-            "scaling": "strong" if wl.name in ("tree-scale", "longctx") else "weak",
-            "vs_baseline": None, "dtype": "f16 in / f32 accumulate",
-            "data": "synthetic (seeded N(0,1) FP16, per-rank seed)", "config": cfg,
-            "e2e": {"value": round(e2e_value, 6), "unit": wl.unit, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h,
-                    "ms_per_step": round(total_e2e / args.steps, 6), "mode": e2e_mode},
-            "gpu_launches": wl.launches * args.steps,
-            "roofline": roof, "clocks": sampler.window(t0, t1), "device_error_word": err,
-        }
-        if world == 1 and not args.no_cpu_baseline:
-            cb = wl.cpu_baseline()
-            cb["value"] = float(f"{cb['value']:.6g}")
-            line["cpu_baseline"] = cb
+        line = {"metric": METRIC, "value": head["value"], "unit": head["unit"],
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "repeats": args.repeats, "ms_per_step": head["ms_per_step"],
+                "higher_is_better": head["higher_is_better"], "scaling": head["scaling"],
+                "vs_baseline": None, "dtype": "f16 in / f32 accumulate",
+                "data": "synthetic (seeded N(0,1) FP16, per-rank seed)"}
+        line.update({k: v for k, v in head.items() if k not in line})
+        line["gpu_launches"] = head["gpu_launches"] + sum(
+            e["gpu_launches"] for e in extras.values())
+        if extras:
+            line["configs"] = extras
         emit(line)
     if world > 1:
         import torch.distributed as dist
@@ -1159,6 +1233,145 @@ def run_ours(args):
 
 
 # --------------------------------------------------------------- reference arm
+def _reference_gpu(torch, O, steps, warmup, repeats):
+    """The reference's own GPU kernels (its src/*.cu compiled unmodified for
+    sm_100a into oracle/_ref/libbcref.so) on the inputs of configs 1-4, each
+    the median of `repeats` regions of `steps` calls, one event pair each."""
+    import bc_capi as C
+    from bc_cow import PagePool
+
+    ref = O.ref()
+    vp = ctypes.c_void_p
+    P = C._ptr
+    stream = torch.cuda.current_stream()
+    st = vp(stream.cuda_stream)
+    device = torch.device("cuda", 0)
+    out = {}
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        ms = [region(torch, fn, steps, stream) for _ in range(repeats)]
+        return statistics.median(ms) / steps
+
+    def shape_of(s):
+        return O.Shape(s.batch, s.query_heads, s.kv_heads, s.dim, s.max_pages, s.physical_pages)
+
+    # config 2: tree verify + the per-request COW commits as the reference's
+    # PagedTreeCache.commit issues them (a page copy, then commit_path)
+    wl = TreeCow(torch, C, device, 0, 1)
+    s = shape_of(wl.shape)
+    pool = PagePool(wl.wl.pool_pages)
+    reqs = [pool.new(wl.wl.prefix)] + [pool.fork(0) for _ in range(wl.wl.batch - 1)]
+    per_req = []
+    page_bytes = 16 * 8 * 128 * 2
+    for b in range(wl.wl.batch):
+        plan = pool.plan_commit_batch([(reqs[b], wl.wl.paths[b], b)], wl.nodes)
+        arr = [torch.tensor(x, dtype=torch.int32, device=device)
+               for x in (plan.entry_node, plan.entry_page, plan.entry_slot)]
+        per_req.append((list(zip(plan.clone_src, plan.clone_dst)), arr))
+    rt = CudaRt()
+    rot = [0]
+
+    def step2():
+        c = rot[0]
+        rot[0] = (c + 1) % wl.copies
+        d = wl.ios[c].dev
+        ck, cv = wl.caches[c]
+        assert ref.bcr_gpu_tree_verify(ctypes.byref(s), wl.nodes, P(d["draft_q"]), P(ck), P(cv),
+                                       P(d["pages"]), P(d["lengths"]), P(d["draft_k"]),
+                                       P(d["draft_v"]), P(d["parent"]), P(wl.outs[c]), st) == 0
+        for b, (clones, (nodes_t, pages_t, slots_t)) in enumerate(per_req):
+            for src, dst in clones:
+                for t in (ck, cv):
+                    rt.copy(t.data_ptr() + dst * page_bytes, t.data_ptr() + src * page_bytes,
+                            page_bytes, 3, st)
+            assert ref.bcr_gpu_commit_path(ctypes.byref(s), P(d["draft_k"]), P(d["draft_v"]),
+                                           P(ck), P(cv), P(nodes_t), P(pages_t), P(slots_t), b,
+                                           wl.nodes, int(nodes_t.numel()), st) == 0
+
+    ms = timed(step2)
+    out["tree-cow"] = {"ms_per_step": round(ms, 6), "value": round(wl.step_bytes / ms / 1e9, 6),
+                       "unit": "TB/s",
+                       "what": "reference tree_kernel + per request a page copy and "
+                               "commit_kernel (8 commit launches, 14 page copies)"}
+    wl.release()
+
+    # config 1 (the reference returns FP32; ours is timed with FP16 output)
+    wl = TreeOracle(torch, C, device, 0, 1)
+    s = shape_of(wl.shape)
+    out32 = torch.empty(wl.out_shape, device=device)
+    rot[0] = 0
+
+    def step1():
+        c = rot[0]
+        rot[0] = (c + 1) % wl.copies
+        d = wl.ios[c].dev
+        ck, cv = wl.caches[c]
+        assert ref.bcr_gpu_tree_verify(ctypes.byref(s), wl.nodes, P(d["draft_q"]), P(ck), P(cv),
+                                       P(d["pages"]), P(d["lengths"]), P(d["draft_k"]),
+                                       P(d["draft_v"]), P(d["parent"]), P(out32), st) == 0
+
+    ms = timed(step1)
+    out["tree-oracle"] = {"ms_per_step": round(ms, 6),
+                          "value": round(wl.step_bytes / ms / 1e9, 6), "unit": "TB/s",
+                          "what": "reference tree_kernel (FP32 output)"}
+    wl.release()
+
+    # config 3 at 4 x 131072: the reference caps the split count at 16
+    wl = Decode(torch, C, device, 0, 1)
+    s = shape_of(wl.shape)
+    splits = min(16, int(ref.bcr_gpu_auto_splits(ctypes.byref(s), wl.context, 148)))
+    splits = max(splits, 1)
+    pa = torch.empty(splits * wl.batch * 32 * 128, device=device)
+    pml = torch.empty(splits * wl.batch * 32 * 2, device=device)
+
+    def step3():
+        assert ref.bcr_gpu_decode(ctypes.byref(s), P(wl.q), P(wl.k), P(wl.v), P(wl.pages),
+                                  P(wl.lengths), P(wl.out), P(pa), P(pml), splits, st) == 0
+
+    ms = timed(step3)
+    out["decode"] = {"ms_per_step": round(ms, 6), "value": round(wl.batch / ms * 1e3, 3),
+                     "unit": "tokens/s", "splits": splits,
+                     "what": "reference decode_kernel + merge_kernel"}
+    wl.release()
+
+    # config 4: the same values in the reference's packed layout [P, Hkv, 16, 2D]
+    # (V at +D), which the reference kernel requires
+    wl = Packed(torch, C, device, 0, 1)
+    refcache = wl.cache.permute(0, 3, 2, 1, 4).contiguous()  # [nb, 8, 16, 2, 128]
+    wl.cache = None
+    s = shape_of(wl.shape)
+
+    def step4():
+        assert ref.bcr_gpu_packed_decode(ctypes.byref(s), P(wl.q), P(refcache), P(wl.pages),
+                                         P(wl.lengths), P(wl.out), ctypes.c_longlong(8 * 16 * 256),
+                                         ctypes.c_longlong(16 * 256), ctypes.c_longlong(256),
+                                         ctypes.c_float(SCALE), st) == 0
+
+    ms = timed(step4)
+    out["packed"] = {"ms_per_step": round(ms, 6), "value": round(wl.batch / ms * 1e3, 3),
+                     "unit": "tokens/s",
+                     "what": "reference packed_decode_kernel on the [P,Hkv,16,2D] layout"}
+    del refcache
+    wl.release()
+    torch.cuda.empty_cache()
+    return out
+
+
+def _reference_sigs(ref):
+    vp, i, ll, f = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_float
+    ref.bcr_gpu_tree_verify.argtypes = [vp, i] + [vp] * 9 + [vp]
+    ref.bcr_gpu_commit_path.argtypes = [vp] + [vp] * 7 + [i, i, i, vp]
+    ref.bcr_gpu_decode.argtypes = [vp] + [vp] * 8 + [i, vp]
+    ref.bcr_gpu_auto_splits.argtypes = [vp, i, i]
+    ref.bcr_gpu_packed_decode.argtypes = [vp] + [vp] * 5 + [ll, ll, ll, f, vp]
+    for fn in (ref.bcr_gpu_tree_verify, ref.bcr_gpu_commit_path, ref.bcr_gpu_decode,
+               ref.bcr_gpu_auto_splits, ref.bcr_gpu_packed_decode):
+        fn.restype = i
+
+
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
@@ -1208,14 +1421,14 @@ def run_reference(args):
                 break
     total = sum(times)
     value = bytes_ / total / 1e12 if unit == "TB/s" else units / total
-    emit({
+    line = {
         "impl": "reference", "metric": METRIC, "value": float(f"{value:.6g}"), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / len(times) * 1e3, 3), "steps_timed": len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 in / f64 accumulate (reference CPU oracle)",
         "data": "synthetic (seeded N(0,1) FP16, same inputs as the CUDA arm's rank 0)",
-        "config": wl.config(),
+        "config": (TreeCow.config(wl) if args.workload == "tree-cow" else wl.config()),
         "cpu_baseline": {"value": float(f"{value:.6g}"), "unit": unit, "cores": cores,
                          "kind": "reference",
                          "sample": "tree-cow: each step = the full 8-request step (the "
@@ -1225,7 +1438,19 @@ def run_reference(args):
                                    "a bounded slice of the step, scaled linearly"},
         "e2e": {"value": float(f"{value:.6g}"), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    })
+    }
+    if args.workload == "tree-cow":
+        # the headline config's l2/parallelism facts, as our arm states them
+        line["config"]["l2"] = "CPU arm: host memory (no GPU cache involved)"
+        line["config"]["parallelism"] = f"request-sharded x{world}"
+    if device is not None and args.workload == "tree-cow" and not args.no_extras:
+        try:
+            _reference_sigs(O.ref())
+            line["reference_gpu_sm100a"] = _reference_gpu(torch, O, args.steps, args.warmup,
+                                                         args.repeats)
+        except Exception as e:  # reported, never fatal to the CPU arm's line
+            line["reference_gpu_sm100a"] = {"unavailable": f"{type(e).__name__}: {e}"}
+    emit(line)
 
 
 RESULT_OUT = sys.stdout
@@ -1241,8 +1466,12 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--repeats", type=int, default=5,
+                    help="timed regions per measurement (the median is reported)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="tree-cow")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="measure only the chosen workload (no `configs` key)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu-measured DRAM bytes per launch of the dominant kernel, if known")
     ap.add_argument("--batch", type=int, default=0, help="decode/packed batch (0: config's)")
@@ -1253,9 +1482,11 @@ def main():
                     help="CPU seconds after which the reference arm stops timing steps")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = {"tree-cow": 2000, "tree-oracle": 2000}.get(args.workload, 50)
+        args.steps = {"tree-cow": 200, "tree-oracle": 200}.get(args.workload, 20)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
+    if args.repeats < 1:
+        ap.error("--repeats must be at least 1")
     # stdout carries exactly the one JSON line: anything else written to file
     # descriptor 1 (library banners such as NCCL's version line) goes to stderr.
     global RESULT_OUT

@@ -29,7 +29,7 @@ EXPORTS = (
     "bc_decode", "bc_auto_splits", "bc_paged_decode", "bc_paged_decode_partial",
     "bc_tree_verify", "bc_tree_verify_f16", "bc_commit_path", "bc_commit_batch",
     "bc_packed_decode", "bc_packed_decode_kv", "bc_merge_partials",
-    "bc_last_device_error", "bc_version", "bc_decode_static_scratch",
+    "bc_last_device_error", "bc_version", "bc_decode_static_scratch", "bc_merge_gathered",
 )
 
 
@@ -60,6 +60,7 @@ _sigs = {
     "bc_packed_decode": [_SP, _vp, _vp, _vp, _vp, _vp, _ll, _ll, _ll, _f, _vp],
     "bc_packed_decode_kv": [_SP, _vp, _vp, _vp, _vp, _vp, _ll, _ll, _ll, _ll, _f, _i, _vp],
     "bc_merge_partials": [_i, _i, _i, _vp, _vp, _vp, _vp],
+    "bc_merge_gathered": [_i, _i, _i, _i, _vp, _vp, _vp],
     "bc_decode_static_scratch": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "bc_last_device_error": [_i],
     "bc_version": [],
@@ -174,6 +175,14 @@ def merge_partials(partial_ml, partial_a, out, stream=None):
     splits, rows, dim = partial_a.shape
     _check(_lib.bc_merge_partials(splits, rows, dim, _ptr(partial_ml), _ptr(partial_a),
                                   _ptr(out), _stream(stream)), "bc_merge_partials")
+
+
+def merge_gathered(gathered, world, splits, rows, dim, out, stream=None):
+    """Merge of `world` ranks' partial buffers gathered into one tensor
+    ([world, splits*rows*(2+dim)]: each rank's (m, l) pairs, then its
+    accumulators)."""
+    _check(_lib.bc_merge_gathered(world, splits, rows, dim, _ptr(gathered), _ptr(out),
+                                  _stream(stream)), "bc_merge_gathered")
 
 
 def decode_static_scratch(shape: Shape, q, k, v, pages, lengths, output, splits=1,

@@ -484,18 +484,27 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 // FP32 merge of global split partials (reference src/paged_gqa.cu:76-106):
-// one warp per row; partial m is in natural-log units.
+// one warp per row; partial m is in natural-log units. Partial p lives in
+// block p / per_block at block_stride floats times that block index past
+// pml and pa (block_stride 0: one block, the reference scratch layout); a
+// context split across GPUs gathers one block per rank, each rank's
+// (m, l) pairs followed by its accumulators in one buffer.
 template <int D>
 __global__ void __launch_bounds__(128)
-    merge_kernel(int rows, int splits, const float* __restrict__ pml,
-                 const float* __restrict__ pa, float* __restrict__ out) {
+    merge_kernel(int rows, int splits, int per_block, long long block_stride,
+                 const float* __restrict__ pml, const float* __restrict__ pa,
+                 float* __restrict__ out) {
   constexpr int R = D / 32;
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
   grid_dependency_wait();  // the partials of the preceding kernel are visible
   if (row >= rows) return;
+  auto at = [&](int s, size_t width) -> size_t {  // offset of partial s's row
+    const int blk = s / per_block, sb = s % per_block;
+    return size_t(blk) * size_t(block_stride) + (size_t(sb) * rows + row) * width;
+  };
   float mmax = -INFINITY;
-  for (int s = 0; s < splits; ++s) mmax = fmaxf(mmax, pml[(size_t(s) * rows + row) * 2]);
+  for (int s = 0; s < splits; ++s) mmax = fmaxf(mmax, pml[at(s, 2)]);
   float acc[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = 0.f;
@@ -507,11 +516,11 @@ __global__ void __launch_bounds__(128)
   }
   float denom = 0.f;
   for (int s = 0; s < splits; ++s) {
-    const size_t sr = size_t(s) * rows + row;
-    const float w = __expf(pml[sr * 2] - mmax);
-    denom += w * pml[sr * 2 + 1];
+    const size_t ml = at(s, 2), a = at(s, D);
+    const float w = __expf(pml[ml] - mmax);
+    denom += w * pml[ml + 1];
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] += w * pa[sr * D + r * 32 + lane];
+    for (int r = 0; r < R; ++r) acc[r] += w * pa[a + r * 32 + lane];
   }
 #pragma unroll
   for (int r = 0; r < R; ++r) o[r * 32 + lane] = acc[r] / denom;

@@ -129,7 +129,9 @@ bool encode_draft_map(CUtensorMap* map, const void* base, int dim, int heads, in
 // FP32 merge of split partials, a programmatic dependent of the kernel that
 // wrote them.
 cudaError_t launch_merge(int dim, int rows, int splits, const float* pml, const float* pa,
-                         float* out, cudaStream_t stream) {
+                         float* out, cudaStream_t stream, int per_block = 0,
+                         long long block_stride = 0) {
+  if (per_block <= 0) per_block = splits;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -139,8 +141,10 @@ cudaError_t launch_merge(int dim, int rows, int splits, const float* pml, const 
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return dim == 64 ? cudaLaunchKernelEx(&cfg, merge_kernel<64>, rows, splits, pml, pa, out)
-                   : cudaLaunchKernelEx(&cfg, merge_kernel<128>, rows, splits, pml, pa, out);
+  return dim == 64 ? cudaLaunchKernelEx(&cfg, merge_kernel<64>, rows, splits, per_block,
+                                        block_stride, pml, pa, out)
+                   : cudaLaunchKernelEx(&cfg, merge_kernel<128>, rows, splits, per_block,
+                                        block_stride, pml, pa, out);
 }
 
 template <int D, int RT, bool OUT_HALF>
@@ -677,6 +681,18 @@ int bc_merge_partials(int splits, int rows, int dim, const float* partial_ml,
     return cudaErrorInvalidValue;
   return launch_merge(dim, rows, splits, partial_ml, partial_a, out,
                       static_cast<cudaStream_t>(stream));
+}
+
+int bc_merge_gathered(int world, int splits, int rows, int dim, const float* gathered,
+                      float* out, void* stream) {
+  if (world < 1 || splits < 1 || rows < 1 || (dim != 64 && dim != 128) || !gathered || !out ||
+      (long long)world * splits > 0x7fffffffLL)
+    return cudaErrorInvalidValue;
+  // rank r's block: splits*rows (m, l) pairs, then splits*rows*dim accumulators
+  const long long ml_floats = (long long)splits * rows * 2;
+  const long long block = ml_floats + (long long)splits * rows * dim;
+  return launch_merge(dim, rows, world * splits, gathered, gathered + ml_floats, out,
+                      static_cast<cudaStream_t>(stream), splits, block);
 }
 
 // ---------------------------------------------------------------------------

@@ -159,6 +159,16 @@ int bc_packed_decode_kv(const bc_shape* shape, const void* q, const void* packed
 int bc_merge_partials(int splits, int rows, int dim, const float* partial_ml,
                       const float* partial_a, float* out, void* stream);
 
+/* bc_merge_partials over partials gathered from `world` GPUs in ONE buffer:
+ * gathered holds `world` blocks back to back, block r being rank r's
+ * bc_paged_decode_partial output with partial_ml and partial_a placed in one
+ * allocation: splits*rows*2 (m, l) floats, then splits*rows*dim accumulator
+ * floats. A single all-gather of each rank's block then feeds the merge of
+ * world*splits partials into out [rows, dim]. Not in the reference; the merge
+ * math is the reference merge_kernel's (src/paged_gqa.cu:76-106). */
+int bc_merge_gathered(int world, int splits, int rows, int dim, const float* gathered,
+                      float* out, void* stream);
+
 /* As bc_paged_decode but writing this call's un-merged state as partials
  * (m, l, acc) per (request, q-head) into partial_ml / partial_a, in the layout
  * of bc_merge_partials with rows = B*Hq: the per-GPU half of a context split

@@ -32,3 +32,14 @@ def test_window_short_region_bracketed():
 def test_window_unsampled():
     w = _sampler([]).window(0.0, 1.0)
     assert w["samples"] == 0 and w["reasons"] == ["unsampled"]
+
+
+def test_bracketing_reasons_kept_apart():
+    """One sample inside the region and a throttled sample just after it: the
+    region's reasons come from the inside sample alone; the bracketing
+    samples' reasons are listed separately."""
+    c = _sampler([(0.0, _row(1965)), (0.1, _row(1965)), (0.2, _row(1700, thermal="Active"))])
+    w = c.window(0.05, 0.15)
+    assert w["bracketing"] and w["samples_inside"] == 1
+    assert w["reasons"] == []
+    assert w["reasons_bracketing"] == ["sw_thermal_slowdown"]

@@ -1,8 +1,9 @@
 """The multi-GPU host logic on CPU ranks (gloo, world size 2): request
 sharding covers every request once, and the split-KV exchange protocol of
-bc_dist (per-rank FP32 (m, l, acc) partials -> all-gather -> merge) gives the
-unsplit decode. The partials here come from a numpy restatement; on GPUs the
-same protocol runs with the CUDA entry points and NCCL."""
+bc_dist (per-rank FP32 (m, l, acc) partials in one buffer -> one all-gather ->
+merge) gives the unsplit decode. The partials here come from a numpy
+restatement; on GPUs the same protocol runs with the CUDA entry points and
+NCCL. The failure tests are in test_dist_failure_cpu.py."""
 import os
 import socket
 
@@ -12,7 +13,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from bc_dist import shard_pages, shard_requests, split_kv_decode
+from bc_dist import block_floats, block_views, shard_pages, shard_requests, split_kv_decode
 
 
 def test_shard_requests_partition():
@@ -64,35 +65,36 @@ def _worker(rank, world, port, data, result):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         q, k, v, pages, length, dim, per_rank = data
+        hq = q.shape[0]
         shard = shard_pages(len(pages), world, rank)
         my_pages = pages[shard.start:shard.stop]
 
         def local():
             # `per_rank` partials per row: this rank's pages split again, as a
-            # GPU keeping its on-chip splits unmerged does.
-            mls, accs = [], []
-            for sub in shard_pages(len(my_pages), per_rank, 0), shard_pages(len(my_pages),
-                                                                            per_rank, 1):
-                if len(mls) == per_rank:
-                    break
+            # GPU keeping its on-chip splits unmerged does, in one buffer.
+            buf = torch.zeros(block_floats(per_rank, hq, dim))
+            pml, pa = block_views(buf, per_rank, hq, dim)
+            for i in range(per_rank):
+                sub = shard_pages(len(my_pages), per_rank, i)
                 start = shard.start + sub.start
                 n = max(0, min(length - start * 16, len(sub) * 16))
-                pml, pa = _partial_numpy(q, k, v, my_pages[sub.start:sub.stop], n, dim)
-                mls.append(torch.from_numpy(pml))
-                accs.append(torch.from_numpy(pa))
-            if per_rank == 1:
-                return mls[0], accs[0]
-            return torch.stack(mls), torch.stack(accs)
+                ml, a = _partial_numpy(q, k, v, my_pages[sub.start:sub.stop], n, dim)
+                pml[i] = torch.from_numpy(ml)
+                pa[i] = torch.from_numpy(a)
+            return buf
 
         def gather(t):
             out = [torch.empty_like(t) for _ in range(world)]
             dist.all_gather(out, t)
             return torch.stack(out)
 
-        def merge(g_ml, g_a):
-            return torch.from_numpy(_merge_numpy(g_ml.numpy(), g_a.numpy()).astype(np.float32))
+        def merge(g):
+            mls, accs = zip(*[block_views(g[r], per_rank, hq, dim) for r in range(world)])
+            g_ml = torch.cat(mls).numpy()
+            g_a = torch.cat(accs).numpy()
+            return torch.from_numpy(_merge_numpy(g_ml, g_a).astype(np.float32))
 
-        out = split_kv_decode(local, merge, gather, q.shape[0], dim, world)
+        out = split_kv_decode(local, merge, gather, per_rank, hq, dim, world)
         result[rank] = out.numpy()
     finally:
         dist.destroy_process_group()

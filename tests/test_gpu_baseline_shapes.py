@@ -239,29 +239,26 @@ def test_config5b_one_gpu_decode(capi, million_context):
 @pytest.mark.parametrize("world", [2, 8])
 def test_config5b_split_across_emulated_ranks(capi, million_context, world):
     """The 1M-token context split into `world` contiguous page shards, one
-    bc_paged_decode_partial per shard (37 unmerged partials per q-head, as the
-    bench runs it), the partials stacked as the all-gather delivers them and
-    reduced by one bc_merge_partials."""
-    from bc_dist import shard_pages
+    bc_paged_decode_partial per shard into one partial buffer (37 unmerged
+    partials per q-head, as the bench runs it), the buffers stacked as the
+    all-gather delivers them and reduced by one bc_merge_gathered."""
+    from bc_dist import block_floats, block_views, shard_pages
 
     c = million_context
     splits = 37
-    partial_ml, partial_a = [], []
+    blocks = []
     capi.last_device_error()
     for r in range(world):
         shard = shard_pages(c["npg"], world, r)
         pages = c["pages"][:, shard.start:shard.stop].contiguous()
         length = torch.tensor([len(shard) * 16], device="cuda", dtype=torch.int32)
         s = capi.make_shape(1, HQ, HKV, D, len(shard), c["P"])
-        pml = torch.full((splits, HQ, 2), float("nan"), device="cuda")
-        pa = torch.full((splits, HQ, D), float("nan"), device="cuda")
+        buf = torch.full((block_floats(splits, HQ, D),), float("nan"), device="cuda")
+        pml, pa = block_views(buf, splits, HQ, D)
         capi.paged_decode_partial(s, c["q"], c["k"], c["v"], pages, length, pml, pa, splits)
-        partial_ml.append(pml)
-        partial_a.append(pa)
-    g_ml = torch.stack(partial_ml).view(world * splits, HQ, 2)
-    g_a = torch.stack(partial_a).view(world * splits, HQ, D)
+        blocks.append(buf)
     out = torch.full((HQ, D), float("nan"), device="cuda")
-    capi.merge_partials(g_ml, g_a, out)
+    capi.merge_gathered(torch.stack(blocks), world, splits, HQ, D, out)
     torch.cuda.synchronize()
     got = out.view(1, HQ, D).cpu().numpy()
     U.assert_close_baseline(got, c["expected"])

@@ -1,8 +1,8 @@
 """One context split across GPUs (BASELINE config 5b), emulated on one GPU.
 
 Each emulated rank owns a contiguous shard of the request's pages and runs
-bc_paged_decode_partial on it; the partials are stacked (the all-gather) and
-bc_merge_partials reduces them. The result must equal the oracle's unsplit
+bc_paged_decode_partial on it into one partial buffer; the buffers are stacked
+(the all-gather) and bc_merge_gathered reduces them. The result must equal the oracle's unsplit
 decode of the whole context. Every rank's kernel runs to completion on its
 own; there is no inter-kernel wait, so emulating the ranks as successive
 launches is exact. The NCCL exchange itself is covered on CPU ranks (gloo) in
@@ -14,7 +14,7 @@ import torch
 
 import bc_testutil as U
 import oracle as O
-from bc_dist import shard_pages, split_kv_decode
+from bc_dist import block_floats, block_views, shard_pages, split_kv_decode
 
 pytestmark = pytest.mark.gpu
 
@@ -45,27 +45,22 @@ def test_split_context_matches_unsplit_oracle(world, splits):
     B, hq, _, dim, _, P = f["shape"]
     rows = B * hq
     S = splits if splits > 8 else 1
-    partials = []
+    blocks = []
     for r in range(world):
         pages, length = _shard_inputs(f, world, r)
         s = C.make_shape(B, hq, 8, dim, pages.shape[1], P)
-        pml = torch.full((S, rows, 2), float("nan"), device="cuda")
-        pa = torch.full((S, rows, dim), float("nan"), device="cuda")
+        buf = torch.full((block_floats(S, rows, dim),), float("nan"), device="cuda")
+        pml, pa = block_views(buf, S, rows, dim)
         C.paged_decode_partial(s, q, k, v, U.to_dev(pages), U.to_dev(length), pml, pa, splits)
-        partials.append((pml, pa))
+        blocks.append(buf)
 
-    calls = iter(range(2))
-
-    def gather(t):
-        i = next(calls)
-        return torch.stack([p[i] for p in partials])
-
-    def merge(g_ml, g_a):
+    def merge(g):
         out = torch.empty(rows, dim, device="cuda")
-        C.merge_partials(g_ml, g_a, out)
+        C.merge_gathered(g, world, S, rows, dim, out)
         return out
 
-    out = split_kv_decode(lambda: partials[0], merge, gather, rows, dim, world)
+    out = split_kv_decode(lambda: blocks[0], merge, lambda t: torch.stack(blocks), S, rows,
+                          dim, world)
     torch.cuda.synchronize()
     got = out.view(B, hq, dim).cpu().numpy()
     assert np.isfinite(got).all()
