@@ -306,8 +306,9 @@ class TreeCow(Workload):
     is far below L2, so the bench rotates over `copies` independent copies of
     all of it, more than twice the L2 size in total: each step touches data
     last used `copies` steps earlier (cold in L2) and no flush kernel runs
-    between steps. Device steps are replayed from one CUDA graph per copy,
-    each holding the step's two C-ABI calls (bc_tree_verify, bc_commit_batch)."""
+    between steps. A step is ONE C-ABI call, bc_tree_verify_commit (the batch
+    commit fused into the verify launch); device steps are replayed from one
+    CUDA graph per copy holding that call."""
 
     name = "tree-cow"
     unit = "TB/s"
@@ -332,12 +333,14 @@ class TreeCow(Workload):
         self.out_shape = (wl.batch, wl.nodes, wl.hq, wl.dim)
         self.out_dtype = torch.float32
         self.nodes = wl.nodes
-        ncl, nent = len(plan.clone_src), len(plan.entry_node)
-        # tree verify + one commit launch (two beyond 256 clones)
-        self.launches = 1 + (0 if ncl + nent == 0 else 1 if ncl <= 256 else 1 + bool(nent))
+        # One launch per step: bc_tree_verify_commit runs the batch commit
+        # (7 clones, 23 rows) on idle warps of the verify kernel.
+        self.fused = len(plan.clone_src) <= 256
+        self.launches = 1 if self.fused else 3
         self.step_bytes = wl.verify_bytes() + wl.commit_bytes(plan)
-        self.kernel_bytes = wl.verify_bytes()
-        self.kernel = "tree_mma_kernel (tree_verify)"
+        self.kernel_bytes = self.step_bytes if self.fused else wl.verify_bytes()
+        self.kernel = ("tree_mma_kernel (tree_verify + the fused COW commit)" if self.fused
+                       else "tree_mma_kernel (tree_verify)")
         self.bound = "hbm"
         self._make_copies(*wl.initial_cache())
 
@@ -372,22 +375,33 @@ class TreeCow(Workload):
             tv = (ctypes.byref(self.shape), P(d["draft_q"]), P(ck), P(cv), P(d["pages"]),
                   P(d["lengths"]), P(d["draft_k"]), P(d["draft_v"]), P(d["parent"]),
                   P(self.outs[c]), self.nodes, st)
-            cb = None
+            cb = fv = None
             if "clone_src" in d:
                 cb = (ctypes.byref(self.shape), self.nodes, P(d["draft_k"]), P(d["draft_v"]),
                       P(ck), P(cv), P(d["clone_src"]), P(d["clone_dst"]),
                       int(d["clone_src"].numel()), P(d["e_req"]), P(d["e_node"]),
                       P(d["e_page"]), P(d["e_slot"]), int(d["e_node"].numel()), st)
+                fv = (ctypes.byref(self.shape), P(d["draft_q"]), P(ck), P(cv), P(d["pages"]),
+                      P(d["lengths"]), P(d["draft_k"]), P(d["draft_v"]), P(d["parent"]),
+                      P(self.outs[c]), int(self.out_dtype == self.torch.float16), self.nodes,
+                      P(d["clone_src"]), P(d["clone_dst"]), int(d["clone_src"].numel()),
+                      P(d["e_req"]), P(d["e_node"]), P(d["e_page"]), P(d["e_slot"]),
+                      int(d["e_node"].numel()), st)
             fn = (C.lib().bc_tree_verify_f16 if self.out_dtype == self.torch.float16
                   else C.lib().bc_tree_verify)
-            self._argv[key] = (fn, tv, cb)
+            self._argv[key] = (fn, tv, cb, fv)
         return self._argv[key]
 
     def launch(self, c, stream=None, verify_only=False):
-        fn, tv, cb = self._args(c, stream or self.torch.cuda.current_stream())
-        rc = fn(*tv)
-        if cb is not None and rc == 0 and not verify_only:
-            rc = self.C.lib().bc_commit_batch(*cb)
+        """One step on copy c: the fused verify + commit call (one foreign
+        call, one launch), or bc_tree_verify then bc_commit_batch."""
+        fn, tv, cb, fv = self._args(c, stream or self.torch.cuda.current_stream())
+        if fv is not None and getattr(self, "fused", False) and not verify_only:
+            rc = self.C.lib().bc_tree_verify_commit(*fv)
+        else:
+            rc = fn(*tv)
+            if cb is not None and rc == 0 and not verify_only:
+                rc = self.C.lib().bc_commit_batch(*cb)
         if rc != 0:
             raise self.C.BranchcraftError(f"bench step failed with cudaError {rc}")
 
@@ -413,7 +427,8 @@ class TreeCow(Workload):
             self.launch(c)
 
     def kernel_step(self):
-        self.launch(self._next(), verify_only=True)
+        # the step's one kernel (verify + fused commit), or the verify alone
+        self.launch(self._next(), verify_only=not getattr(self, "fused", False))
 
     def e2e_step(self):
         c = self._next()
@@ -955,8 +970,9 @@ class TreeScale(Workload):
 class LongCtx(Workload):
     """BASELINE config 5b: one request of 1,048,576 tokens; rank r holds a
     contiguous 1/world shard of its pages and reduces it to FP32 partials
-    (m, l, acc) — `splits` of them per q-head, unmerged, when splits > 8 — in
-    ONE buffer, which a single NCCL all-gather brings to every rank, where one
+    (m, l, acc) — `splits` of them per q-head when splits > 8, which a second
+    launch reduces to one partial per q-head (16,640 bytes per rank) — in ONE
+    buffer, which a single NCCL all-gather brings to every rank, where one
     launch merges all of them (bc_merge_gathered). value = tokens/s (one
     decoded token per job step); strong scaling."""
 
@@ -988,14 +1004,20 @@ class LongCtx(Workload):
         self.q_host = torch.randn(1, 32, 128, dtype=torch.float16, generator=gq).pin_memory()
         self.q = self.q_host.to(device)
         self.out_host = torch.empty(1, 32, 128).pin_memory()
-        self.buf = torch.empty(block_floats(self.S, 32, 128), device=device)
-        self.pml, self.pa = block_views(self.buf, self.S, 32, 128)
+        # this rank's splits; with more than one rank they are reduced to ONE
+        # partial per row (bc_merge_to_partial) in the buffer that is gathered
+        self.part = torch.empty(block_floats(self.S, 32, 128), device=device)
+        self.pml, self.pa = block_views(self.part, self.S, 32, 128)
+        self.buf = torch.empty(block_floats(1, 32, 128), device=device)
+        self.send_ml, self.send_a = block_views(self.buf, 1, 32, 128)
         self.gathered = torch.empty(world, self.buf.numel(), device=device)
         self.out = torch.empty(32, 128, device=device)
         self.total = total
         self.kernel_bytes = npg * 16 * 4096 + 32 * 128 * 2 + self.S * 32 * 130 * 4
         self.step_bytes = self.kernel_bytes
-        self.launches = 2  # rank-local partial decode + merge of every rank's partials
+        # partial decode, (world > 1: local reduction to one partial, one NCCL
+        # all-gather,) merge of every rank's partials
+        self.launches = 2 + (world > 1 and self.S > 1)
         self.kernel = "attn_kernel (paged decode partial)"
         self.bound = "hbm"
         self.group = None
@@ -1013,11 +1035,14 @@ class LongCtx(Workload):
         if self.world > 1:
             import torch.distributed as dist
 
+            if self.S > 1:
+                self.C.merge_to_partial(self.pml, self.pa, self.send_ml[0], self.send_a[0])
+            else:
+                self.buf.copy_(self.part)
             dist.all_gather_into_tensor(self.gathered, self.buf, group=self.group)
-            g = self.gathered
+            self.C.merge_gathered(self.gathered, self.world, 1, 32, 128, self.out)
         else:
-            g = self.buf.view(1, -1)
-        self.C.merge_gathered(g, self.world, self.S, 32, 128, self.out)
+            self.C.merge_gathered(self.part.view(1, -1), 1, self.S, 32, 128, self.out)
 
     def e2e_step(self):
         self.q.copy_(self.q_host, non_blocking=True)
@@ -1036,7 +1061,7 @@ class LongCtx(Workload):
                             "one buffer per rank) and merged on the device",
                 "tokens_per_gpu": int(self.lengths[0]), "splits_per_gpu": self.splits,
                 "parallelism": f"context-split x{self.world}",
-                "collective_bytes_per_rank": self.buf.numel() * 4}
+                "collective_bytes_per_rank": self.buf.numel() * 4 if self.world > 1 else 0}
 
     def release(self):
         if getattr(self, "group", None) is not None:

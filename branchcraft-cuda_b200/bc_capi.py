@@ -30,6 +30,7 @@ EXPORTS = (
     "bc_tree_verify", "bc_tree_verify_f16", "bc_commit_path", "bc_commit_batch",
     "bc_packed_decode", "bc_packed_decode_kv", "bc_merge_partials",
     "bc_last_device_error", "bc_version", "bc_decode_static_scratch", "bc_merge_gathered",
+    "bc_merge_to_partial", "bc_tree_verify_commit",
 )
 
 
@@ -57,10 +58,13 @@ _sigs = {
     "bc_tree_verify_f16": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "bc_commit_path": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
     "bc_commit_batch": [_SP, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _vp],
+    "bc_tree_verify_commit": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i,
+                              _vp, _vp, _i, _vp, _vp, _vp, _vp, _i, _vp],
     "bc_packed_decode": [_SP, _vp, _vp, _vp, _vp, _vp, _ll, _ll, _ll, _f, _vp],
     "bc_packed_decode_kv": [_SP, _vp, _vp, _vp, _vp, _vp, _ll, _ll, _ll, _ll, _f, _i, _vp],
     "bc_merge_partials": [_i, _i, _i, _vp, _vp, _vp, _vp],
     "bc_merge_gathered": [_i, _i, _i, _i, _vp, _vp, _vp],
+    "bc_merge_to_partial": [_i, _i, _i, _vp, _vp, _vp, _vp, _vp],
     "bc_decode_static_scratch": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "bc_last_device_error": [_i],
     "bc_version": [],
@@ -156,6 +160,21 @@ def commit_batch(shape, nodes, draft_k, draft_v, cache_k, cache_v, clone_src, cl
            "bc_commit_batch")
 
 
+def tree_verify_commit(shape, draft_q, cache_k, cache_v, pages, lengths, draft_k, draft_v,
+                       parent, output, nodes, clone_src, clone_dst, entry_request, entry_node,
+                       entry_page, entry_slot, stream=None):
+    """tree_verify and the batch copy-on-write commit in one launch (the
+    commit plan must be a copy-on-write plan: see bc_tree_verify_commit)."""
+    nclones = 0 if clone_src is None else int(clone_src.numel())
+    nentries = 0 if entry_node is None else int(entry_node.numel())
+    _check(_lib.bc_tree_verify_commit(
+        ctypes.byref(shape), _ptr(draft_q), _ptr(cache_k), _ptr(cache_v), _ptr(pages),
+        _ptr(lengths), _ptr(draft_k), _ptr(draft_v), _ptr(parent), _ptr(output),
+        1 if output.dtype == torch.float16 else 0, nodes, _ptr(clone_src), _ptr(clone_dst),
+        nclones, _ptr(entry_request), _ptr(entry_node), _ptr(entry_page), _ptr(entry_slot),
+        nentries, _stream(stream)), "bc_tree_verify_commit")
+
+
 def packed_decode(shape, q, packed_kv, pages, lengths, output, block_stride, head_stride,
                   slot_stride, scale, stream=None):
     _check(_lib.bc_packed_decode(ctypes.byref(shape), _ptr(q), _ptr(packed_kv), _ptr(pages),
@@ -175,6 +194,15 @@ def merge_partials(partial_ml, partial_a, out, stream=None):
     splits, rows, dim = partial_a.shape
     _check(_lib.bc_merge_partials(splits, rows, dim, _ptr(partial_ml), _ptr(partial_a),
                                   _ptr(out), _stream(stream)), "bc_merge_partials")
+
+
+def merge_to_partial(partial_ml, partial_a, out_ml, out_a, stream=None):
+    """Merge [S, rows, *] partials into ONE partial per row: (M, L) into
+    out_ml [rows, 2], the unnormalised accumulator into out_a [rows, dim]."""
+    splits, rows, dim = partial_a.shape
+    _check(_lib.bc_merge_to_partial(splits, rows, dim, _ptr(partial_ml), _ptr(partial_a),
+                                    _ptr(out_ml), _ptr(out_a), _stream(stream)),
+           "bc_merge_to_partial")
 
 
 def merge_gathered(gathered, world, splits, rows, dim, out, stream=None):

@@ -6,7 +6,8 @@ and page table) and reduces it to partial softmax states per (request,
 q-head): (m, l) and the unnormalised accumulator, in FP32. A rank's partials
 sit in ONE buffer — its `splits * rows` (m, l) pairs, then its
 `splits * rows * dim` accumulators — so a single NCCL all-gather of that
-buffer (16,640 bytes per rank and split for Hq=32, D=128) brings every rank's
+buffer (one partial per row: 16,640 bytes per rank for Hq=32, D=128; a rank
+first reduces its own on-device splits with bc_merge_to_partial) brings every rank's
 partials to every rank, where one merge launch (bc_merge_gathered, the math of
 the reference merge_kernel, src/paged_gqa.cu:76-106) reduces them. Requests
 that fit on one GPU are instead sharded by request with no collective at all
@@ -191,9 +192,9 @@ def cuda_split_kv_decode(shape, q, k, v, pages, lengths, group=None, splits: int
     """Production path: bc_paged_decode_partial on this rank's shard into one
     partial buffer, one NCCL all_gather_into_tensor of it, bc_merge_gathered.
     `shape`, `pages`, `lengths` describe this rank's shard; returns FP32
-    [B, Hq, D] on every rank. `splits` > 8 keeps that many unmerged partials
-    per row on every rank (all gathered and merged at once); otherwise each
-    rank sends one. With `gate`, every rank passes the step gate first; with
+    [B, Hq, D] on every rank. `splits` > 8 runs that many splits on the rank
+    (global partials, reduced on the rank by bc_merge_to_partial); every rank
+    sends one partial per row either way. With `gate`, every rank passes the step gate first; with
     `deadline_s` > 0 the collective is waited for under that host deadline
     (the host then synchronises with the step)."""
     import torch
@@ -209,9 +210,15 @@ def cuda_split_kv_decode(shape, q, k, v, pages, lengths, group=None, splits: int
         gate.enter(step)
 
     def local_partial():
-        buf = torch.empty(block_floats(S, rows, shape.dim), device=dev, dtype=torch.float32)
-        pml, pa = block_views(buf, S, rows, shape.dim)
+        part = torch.empty(block_floats(S, rows, shape.dim), device=dev, dtype=torch.float32)
+        pml, pa = block_views(part, S, rows, shape.dim)
         C.paged_decode_partial(shape, q, k, v, pages, lengths, pml, pa, splits)
+        if S == 1:
+            return part
+        # the rank's splits reduced to ONE partial per row before the exchange
+        buf = torch.empty(block_floats(1, rows, shape.dim), device=dev, dtype=torch.float32)
+        ml1, a1 = block_views(buf, 1, rows, shape.dim)
+        C.merge_to_partial(pml, pa, ml1[0], a1[0])
         return buf
 
     def all_gather(t):
@@ -223,8 +230,8 @@ def cuda_split_kv_decode(shape, q, k, v, pages, lengths, group=None, splits: int
 
     def merge(g):
         out = torch.empty(rows, shape.dim, device=dev, dtype=torch.float32)
-        C.merge_gathered(g, world, S, rows, shape.dim, out)
+        C.merge_gathered(g, world, 1, rows, shape.dim, out)
         return out
 
-    out = split_kv_decode(local_partial, merge, all_gather, S, rows, shape.dim, world)
+    out = split_kv_decode(local_partial, merge, all_gather, 1, rows, shape.dim, world)
     return out.view(shape.batch, shape.query_heads, shape.dim)

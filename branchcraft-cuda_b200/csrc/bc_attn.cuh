@@ -489,11 +489,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 // pml and pa (block_stride 0: one block, the reference scratch layout); a
 // context split across GPUs gathers one block per rank, each rank's
 // (m, l) pairs followed by its accumulators in one buffer.
-template <int D>
+// TO_PARTIAL: instead of the normalised row, store the merged state itself —
+// (M, L) at out_ml[row] and the unnormalised accumulator at out[row], every
+// partial weighted by exp(m_p - M) — one partial per row for a later merge
+// (all-empty rows: M = -inf, L = 0, accumulator 0).
+template <int D, bool TO_PARTIAL = false>
 __global__ void __launch_bounds__(128)
     merge_kernel(int rows, int splits, int per_block, long long block_stride,
                  const float* __restrict__ pml, const float* __restrict__ pa,
-                 float* __restrict__ out) {
+                 float* __restrict__ out, float* __restrict__ out_ml) {
   constexpr int R = D / 32;
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -512,6 +516,10 @@ __global__ void __launch_bounds__(128)
   if (mmax == -INFINITY) {
 #pragma unroll
     for (int r = 0; r < R; ++r) o[r * 32 + lane] = 0.f;
+    if (TO_PARTIAL && lane == 0) {
+      out_ml[size_t(row) * 2] = -INFINITY;
+      out_ml[size_t(row) * 2 + 1] = 0.f;
+    }
     return;
   }
   float denom = 0.f;
@@ -522,8 +530,17 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[r] += w * pa[a + r * 32 + lane];
   }
+  if constexpr (TO_PARTIAL) {
 #pragma unroll
-  for (int r = 0; r < R; ++r) o[r * 32 + lane] = acc[r] / denom;
+    for (int r = 0; r < R; ++r) o[r * 32 + lane] = acc[r];
+    if (lane == 0) {
+      out_ml[size_t(row) * 2] = mmax;
+      out_ml[size_t(row) * 2 + 1] = denom;
+    }
+  } else {
+#pragma unroll
+    for (int r = 0; r < R; ++r) o[r * 32 + lane] = acc[r] / denom;
+  }
 }
 
 }  // namespace bc

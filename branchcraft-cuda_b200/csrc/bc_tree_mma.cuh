@@ -53,6 +53,7 @@
 #pragma once
 
 #include "bc_attn.cuh"
+#include "bc_commit.cuh"
 
 namespace bc {
 
@@ -77,6 +78,7 @@ struct TreeRegs {
                 "setmaxnreg takes multiples of 8 in [24, 256]");
 };
 constexpr int kTreeMaxReq = 128;     // requests per CTA (rows per request >= 1)
+constexpr int kPrologueThreads = 256;  // warps 0-7 run the prologue's shared-memory phases
 
 struct TreeParams {
   int batch, hq, hkv, group, nodes;
@@ -94,6 +96,23 @@ struct TreeParams {
   void* out;            // [B, N, Hq, D] FP32 or FP16
   float scale_log2;
   unsigned* err;
+  // The batch copy-on-write commit fused into the launch (commit_tasks > 0):
+  // its tasks (commit_batch_task) run on warps 12-15 once their own roles are
+  // done, spread over the grid's CTAs. The commit writes only bytes no
+  // verified row depends on (fresh pages, and slots at or past every reading
+  // request's length: the copy-on-write plan's contract), so it needs no
+  // ordering against the verification.
+  int commit_tasks, nclones, nentries;
+  __half* cache_k;
+  __half* cache_v;
+  const __half* draft_k;
+  const __half* draft_v;
+  const int* clone_src;
+  const int* clone_dst;
+  const int* entry_request;
+  const int* entry_node;
+  const int* entry_page;
+  const int* entry_slot;
 };
 
 // DUAL: one CTA runs two consecutive 128-row tiles of a request block over
@@ -116,13 +135,14 @@ struct TreeGeom {
   static constexpr int kQBytes = kRT * kQTile;
   static constexpr int kBarOff = kQOff + kQBytes;
   static constexpr int kSBufs = 4;  // S/P buffers in TMEM (unit u uses u % 4)
-  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 3 * kSBufs + 2 + 1 + 1;
+  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 3 * kSBufs + 2 + 1 + 1 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   // misc: tmem base (4) + nruns (4) + run tables 6 x kTreeMaxReq ints
   static constexpr int kRunOff = kMiscOff + 16;
   static constexpr int kORowOff = kRunOff + 6 * kTreeMaxReq * 4;  // [kRT*128] output row of each tile row
   static constexpr int kMlXOff = kORowOff + kRT * kTreeRows * 4;  // [2][128][2] each group's (m, l)
-  static constexpr int kParOff = kMlXOff + 2 * kTreeRows * 8;
+  static constexpr int kCommitOff = kMlXOff + 2 * kTreeRows * 8;  // CommitScratch
+  static constexpr int kParOff = kCommitOff + ((int(sizeof(CommitScratch)) + 15) & ~15);
   // Epilogue (after the main loop, reusing the K/V rings): this CTA's output
   // rows at kStageOff, each D FP32 values and a 16-byte trailer holding the
   // row's (m, l) for the cluster merge; for a cluster split, kSlotRows
@@ -173,6 +193,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   uint64_t* mma_done = pv_done + 2;            // [1] the S issuer's last MMA
   uint64_t* s_free = mma_done + 1;             // [3] PV done reading S/P buffer b
   uint64_t* pv_fin = s_free + G::kSBufs;       // [1] the PV issuer's last MMA
+  uint64_t* anc_ready = pv_fin + 1;            // [1] the ancestor sets are written
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + G::kMiscOff);
   int* nruns_s = reinterpret_cast<int*>(smem + G::kMiscOff + 4);
   int* run_first = reinterpret_cast<int*>(smem + G::kRunOff);  // first local request
@@ -219,6 +240,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       mbar_init(&p_full[s], 4);
     }
     mbar_init(pv_fin, 1);
+    mbar_init(anc_ready, 2);  // warps 13 and 15
     for (int s = 0; s < 2; ++s) mbar_init(&pv_done[s], 1);
     mbar_init(mma_done, 1);
     fence_mbar_init();
@@ -237,6 +259,14 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // is bounded per issuing warp).
   const bool producer = warp == 8 || warp == 10 || warp == 12 || warp == 14;
   const int psub = warp >= 12 ? 1 : 0;  // tile parity of a producer warp
+  const bool v_warp = warp == 10 || warp == 14;
+  // The barriers and the TMEM allocation are visible to every warp before any
+  // input is read, so the producers can issue copies before the prologue's
+  // shared-memory phases (still no input read: this may overlap the
+  // preceding kernel).
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
   // A one-wave grid lets the next kernel of the stream be scheduled now: its
   // CTAs take free SMs, run their set-up and wait there for this grid.
   if (p.early_trigger) grid_launch_dependents();
@@ -250,14 +280,19 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   const int ndraft_tiles = (nreq * npad + kTreeTile - 1) / kTreeTile;
   const int npar = nreq * p.nodes;              // <= 256: R * nodes (host)
   const int ncmp = (nreq - 1) * p.max_pages;    // page-row comparisons
-  const int ld_len = tid < nreq ? __ldg(p.lengths + b0 + tid) : 0;
-  const int ld_par = tid < npar ? __ldg(p.parent + size_t(b0) * p.nodes + tid) : 0;
+  // Phases 1 and 2 run on the softmax warps (0-7, kPrologueThreads) behind a
+  // named barrier; the other warps join only at the barrier that ends the
+  // prologue, so the producers' early copies hold nobody up.
+  constexpr int kPT = kPrologueThreads;
+  const bool pro = tid < kPT;
+  const int ld_len = pro && tid < nreq ? __ldg(p.lengths + b0 + tid) : 0;
+  const int ld_par = pro && tid < npar ? __ldg(p.parent + size_t(b0) * p.nodes + tid) : 0;
   int cmp_a[4], cmp_b[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int w = tid + k * kTreeThreads;
+    const int w = tid + k * kPT;
     cmp_a[k] = cmp_b[k] = 0;
-    if (w < ncmp) {
+    if (pro && w < ncmp) {
       const int i = 1 + w / p.max_pages, j = w % p.max_pages;
       cmp_a[k] = __ldg(p.pages + size_t(b0 + i) * p.max_pages + j);
       cmp_b[k] = __ldg(p.pages + size_t(b0 + i - 1) * p.max_pages + j);
@@ -284,41 +319,78 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   }
   // Producer: page ids of tiles 0..15 of this CTA's key range, speculating
   // that the block is one run of request b0's prefix spanning the whole page
-  // table; the producer checks the guess after phase 2.
+  // table (the common shared-prefix case); the guess is checked after phase 2.
+  // Under the guess the CTA's key range is known now, so each producer issues
+  // its first prefix tiles (one pass through its ring, no stage to free) at
+  // once, before the shared-memory phases: their copies land while those run.
+  // The producers end the prologue only once these copies have landed. If
+  // the guess fails, they refill the same stages, every consumer of those
+  // stages then waiting for one phase more (k_phase / v_phase below). Pages
+  // past request b0's length are left out (id -1: the TMA fills zeros),
+  // exactly as the checked path masks them.
   const int spec_t0 = (cap + kTreeTile - 1) / kTreeTile;
+  // The guessed range's first tile and its count of prefix tiles (a function
+  // of the launch parameters only, recomputed where needed).
+  auto spec_range = [&](int& v0s) -> int {
+    const int tot = spec_t0 + ndraft_tiles;
+    const int per = (tot + p.splits - 1) / p.splits;
+    v0s = min(tot, split * per);
+    const int nt = min(tot, v0s + per) - v0s;
+    return max(0, min(nt, spec_t0 - v0s));
+  };
   int cur_ids = -1, next_ids = -1;
   if (producer) {
-    const int tot = spec_t0 + ndraft_tiles;
-    const int per0 = (tot + p.splits - 1) / p.splits;
-    const int spec_v0 = min(tot, split * per0);
-    auto spec_id = [&](int i) -> int {  // i: this warp's i-th tile
+    int spec_v0 = 0;
+    const int spec_pre = spec_range(spec_v0);
+    const int nspec_k = min(spec_pre, G::kKStages);  // local tiles [0, nspec) speculated
+    const int nspec_v = min(spec_pre, G::kVStages);
+    // (the ids are loaded with the length, not after it: one round trip)
+    const int len_raw = __ldg(p.lengths + b0);
+    auto spec_pg = [&](int i) -> int {  // page of this lane in this warp's i-th tile
       const int v = spec_v0 + psub + 2 * i;
-      if (v >= spec_t0) return -1;
       const int pg = v * 4 + (lane & 3);
-      if (pg >= p.max_pages) return -1;
-      return __ldg(p.pages + size_t(b0) * p.max_pages + pg);
+      return v < spec_t0 && pg < p.max_pages ? pg : -1;
     };
-    cur_ids = spec_id(lane >> 2);
-    next_ids = spec_id(8 + (lane >> 2));
+    const int pg_cur = spec_pg(lane >> 2), pg_next = spec_pg(8 + (lane >> 2));
+    cur_ids = pg_cur >= 0 ? __ldg(p.pages + size_t(b0) * p.max_pages + pg_cur) : -1;
+    next_ids = pg_next >= 0 ? __ldg(p.pages + size_t(b0) * p.max_pages + pg_next) : -1;
+    const int len0 = min(max(len_raw, 0), cap);
+    if (pg_cur * kPageSize >= len0) cur_ids = -1;  // past request b0's length
+    if (pg_next * kPageSize >= len0) next_ids = -1;
+    const int nspec = v_warp ? nspec_v : nspec_k;
+    for (int jj = 0, i = psub; i < nspec; ++jj, i += 2) {  // local tile i -> stage i
+      const int page_id = __shfl_sync(0xffffffffu, cur_ids, (jj & 7) * 4 + min(lane / KB, 3));
+      if (!v_warp && lane < 4 * KB && lane % KB == 0 &&
+          (page_id >= p.physical_pages || page_id < -1))
+        atomicOr(p.err, kErrPageRange);
+      uint64_t* full = (v_warp ? v_full : k_full) + i;
+      if (lane == 0) mbar_arrive_expect_tx(full, uint32_t(G::kHalfTile));
+      __syncwarp();
+      if (lane < 4 * KB) {
+        uint8_t* dst = smem + (v_warp ? G::kVOff : G::kKOff) + i * G::kHalfTile +
+                       (lane % KB) * (kTreeTile * 128) + (lane / KB) * 2048;
+        tma_load_4d(dst, v_warp ? &vmap : &kmap, full, (lane % KB) * 64, kvh, 0, page_id);
+      }
+      __syncwarp();
+    }
   }
-  for (int i = tid; i < nreq; i += kTreeThreads) mismatch[i] = 0x7fffffff;
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tbase = *tmem_slot;
   const uint32_t lane_addr = uint32_t((warp & 3) * 32) << 16;  // this warp's TMEM lanes
+  if (pro) {
+  for (int i = tid; i < nreq; i += kPT) mismatch[i] = 0x7fffffff;
+  named_barrier_sync(3, kPT);
 
   // Phase 1: the loaded values into shared memory.
-  for (int i = tid; i < nreq; i += kTreeThreads)
+  for (int i = tid; i < nreq; i += kPT)
     len_s[i] = i == tid ? ld_len : __ldg(p.lengths + b0 + i);
-  for (int e = tid; e < npar; e += kTreeThreads)
+  for (int e = tid; e < npar; e += kPT)
     par_s[e] = e == tid ? ld_par : __ldg(p.parent + size_t(b0) * p.nodes + e);
   // First page where request i's row differs from request i-1's.
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int w = tid + k * kTreeThreads;
+    const int w = tid + k * kPT;
     if (w < ncmp && cmp_a[k] != cmp_b[k]) atomicMin(&mismatch[1 + w / p.max_pages], w % p.max_pages);
   }
-  for (int w = tid + 4 * kTreeThreads; w < ncmp; w += kTreeThreads) {  // very wide tables only
+  for (int w = tid + 4 * kPT; w < ncmp; w += kPT) {  // very wide tables only
     const int i = 1 + w / p.max_pages, j = w % p.max_pages;
     if (__ldg(p.pages + size_t(b0 + i) * p.max_pages + j) !=
         __ldg(p.pages + size_t(b0 + i - 1) * p.max_pages + j))
@@ -335,27 +407,11 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
                    qv[4 * k + 0], qv[4 * k + 1], qv[4 * k + 2], qv[4 * k + 3]);
     fence_proxy_async_smem();  // the rows -> the MMA's reads
   }
-  tc_fence_before();
-  __syncthreads();
+  named_barrier_sync(3, kPT);
 
-  // Phase 2: shared memory only — ancestor sets and runs of identical requests.
-  for (int e = tid; e < nreq * p.nodes; e += kTreeThreads) {
-    const int rq = e / p.nodes, n = e % p.nodes;
-    uint32_t* row = anc + size_t(e) * 8;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) row[w] = 0u;
-    const int* par = par_s + rq * p.nodes;
-    int cur = n, steps = 0;
-    while (cur >= 0) {
-      if (cur >= p.nodes || steps >= p.nodes) {
-        atomicOr(p.err, kErrParent);
-        break;
-      }
-      row[cur >> 5] |= 1u << (cur & 31);
-      cur = par[cur];
-      ++steps;
-    }
-  }
+  // Phase 2: runs of identical requests (the ancestor sets, needed only by
+  // the draft-token tiles at the end of the key range, are written later by
+  // warps 13 and 15 while the first tiles run).
   if (tid == 0) {
     int k = -1, prev_len = 0;
     for (int i = 0; i < nreq; ++i) {
@@ -375,9 +431,38 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     }
     *nruns_s = k + 1;
   }
-  __syncthreads();
+  }  // pro
+  if (producer) {
+    // The speculative copies land before the prologue ends: no consumer can
+    // then wait on a speculated stage before its first phase is complete (a
+    // parity wait cannot tell a failed guess's refill, the phase it wants,
+    // from the speculative phase before it).
+    int v0s = 0;
+    const int nspec = min(spec_range(v0s), v_warp ? G::kVStages : G::kKStages);
+    bool landed = true;
+    for (int i = psub; i < nspec; i += 2)
+      landed = mbar_wait((v_warp ? v_full : k_full) + i, 0) && landed;
+    if (!__all_sync(0xffffffffu, landed) && lane == 0) atomicOr(p.err, kErrTimeout);
+  }
+  tc_fence_before();
+  __syncthreads();  // the end of the prologue
   tc_fence_after();
   const int nruns = *nruns_s;
+  // The speculation held when the block is one run covering the whole table
+  // width: then the CTA's key range is the one the producers guessed. When it
+  // failed, stages [0, nspec) took one speculative fill nobody consumes: a
+  // wait on such a stage's full barrier looks one phase further.
+  const bool spec_ok = nruns == 1 && run_tiles[0] == spec_t0;
+  int spec_v0_unused = 0;
+  const int spec_pre = spec_range(spec_v0_unused);
+  const int nspec_k = min(spec_pre, G::kKStages), nspec_v = min(spec_pre, G::kVStages);
+  const int xk = spec_ok ? 0 : nspec_k, xv = spec_ok ? 0 : nspec_v;  // stages one phase ahead
+  auto k_phase = [xk](int i) -> uint32_t {
+    return uint32_t((i / G::kKStages) + ((i % G::kKStages) < xk ? 1 : 0)) & 1u;
+  };
+  auto v_phase = [xv](int i) -> uint32_t {
+    return uint32_t((i / G::kVStages) + ((i % G::kVStages) < xv ? 1 : 0)) & 1u;
+  };
 
   // ---- this CTA's slice of the key tiles: all runs' prefix tiles, then drafts
   int total = 0;
@@ -487,8 +572,8 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   if (producer) {
     // ------------------------------------------------------------ producers
     // warps 8 / 12: K, warps 10 / 14: V; tiles of parity psub
-    const bool v_warp = warp == 10 || warp == 14;
     constexpr int per_part = 4 * KB;  // boxes per tile
+    const int nspec = v_warp ? nspec_v : nspec_k;  // (landed before the prologue ended)
     if (ntiles > psub) {
       int run, t;
       start_cursor(v0 + psub, run, t);
@@ -560,6 +645,11 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
           cur_ids = next_ids;
           next_ids = load_ids(j + 8);
         }
+        if (spec_ok && i < nspec) {  // issued before the prologue's phases
+          step();
+          step();
+          continue;
+        }
         const bool is_prefix = run < nruns;
         // the page id of this lane's box
         const int page_id = __shfl_sync(0xffffffffu, cur_ids, (j & 7) * 4 + min(lane / KB, 3));
@@ -595,7 +685,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         // S/P buffer sb was last used by unit u-4: its PV must have read P.
         ok = __all_sync(0xffffffffu, (u < G::kSBufs ||
                                       mbar_wait(&s_free[sb], ((u - G::kSBufs) / G::kSBufs) & 1)) &&
-                                         (g != 0 || mbar_wait(&k_full[kst], (i / G::kKStages) & 1)));
+                                         (g != 0 || mbar_wait(&k_full[kst], k_phase(i))));
         if (!ok) break;
         tc_fence_after();
         const uint64_t kdesc = kdesc0 + uint64_t((kst * G::kHalfTile) >> 4);
@@ -632,7 +722,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         const int buf = DUAL ? g : (i & 1);  // the O accumulator (and pv_done) of this unit
         const int sb = u % G::kSBufs;
         ok = __all_sync(0xffffffffu, mbar_wait(&p_full[sb], (u / G::kSBufs) & 1) &&
-                                         (g != 0 || mbar_wait(&v_full[vst], (i / G::kVStages) & 1)));
+                                         (g != 0 || mbar_wait(&v_full[vst], v_phase(i))));
         if (!ok) break;
         tc_fence_after();
         const uint64_t vdesc = vdesc0 + uint64_t((vst * G::kHalfTile) >> 4);
@@ -663,6 +753,45 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       __syncwarp();
       if (!__all_sync(0xffffffffu, mbar_wait(pv_fin, 0)) && lane == 0) atomicOr(p.err, kErrTimeout);
     }
+  }
+  else if (warp == 13 || warp == 15) {
+    // ------------------------------------------------------- ancestor sets
+    // Bit n' of entry (request, node n) is set when n' is n or one of its
+    // ancestors; chains leaving [0, nodes) or longer than `nodes` (a cycle)
+    // stop and set BC_ERR_PARENT.
+    for (int e = (warp == 15 ? 32 : 0) + lane; e < nreq * p.nodes; e += 64) {
+      const int rq = e / p.nodes, n = e % p.nodes;
+      uint32_t* row = anc + size_t(e) * 8;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) row[w] = 0u;
+      const int* par = par_s + rq * p.nodes;
+      int cur = n, steps = 0;
+      while (cur >= 0) {
+        if (cur >= p.nodes || steps >= p.nodes) {
+          atomicOr(p.err, kErrParent);
+          break;
+        }
+        row[cur >> 5] |= 1u << (cur & 31);
+        cur = par[cur];
+        ++steps;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(anc_ready);
+  }
+  if (p.commit_tasks > 0 && warp >= 12) {
+    // ------------------------------------------------------- fused commit
+    // Warps 12-15 (both idle by now: the odd-tile producers have issued
+    // their last copies, the ancestor sets are written) take the CTA's share
+    // of the batch commit's tasks.
+    CommitScratch& sc = *reinterpret_cast<CommitScratch*>(smem + G::kCommitOff);
+    const int ncta = int(gridDim.x * gridDim.z);
+    const int row_halves = p.hkv * D;
+    for (int task = int(blockIdx.x + gridDim.x * blockIdx.z); task < p.commit_tasks; task += ncta)
+      commit_batch_task<128>(task, tid - 384, [] { named_barrier_sync(4, 128); }, sc, row_halves,
+                             p.batch, p.nodes, p.physical_pages, p.draft_k, p.draft_v, p.cache_k,
+                             p.cache_v, p.clone_src, p.clone_dst, p.nclones, p.entry_request,
+                             p.entry_node, p.entry_page, p.entry_slot, p.nentries, p.err);
   }
   // ---- epilogue of warps 8-15: the barriers of the softmax warps' epilogue,
   // the TMEM release, and a share of the owners' sums.
@@ -699,6 +828,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     int run, t;
     start_cursor(v0 + i0, run, t);
     const uint32_t* my_anc = anc + (size_t(max(my_req, 0)) * p.nodes + my_node) * 8;
+    bool anc_seen = false;
     for (int i = i0; i < ntiles; i += di) {
       const int buf = DUAL ? wg : (i & 1);   // this group's O accumulator
       const int u = DUAL ? 2 * i + wg : i;   // the S/P unit
@@ -742,6 +872,13 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         for (int c = 0; c < 64; ++c)
           x[c] = (in_run && c < valid_keys) ? __uint_as_float(s[c]) : kNegInf;
       } else {
+        if (!anc_seen) {  // (one phase only: the first draft tile waits)
+          if (!mbar_wait(anc_ready, 0)) {
+            softmax_ok = false;
+            break;
+          }
+          anc_seen = true;
+        }
         const int slot0 = t * kTreeTile;
 #pragma unroll
         for (int c = 0; c < 64; c += 16) {
@@ -811,7 +948,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
       if (is_prefix && valid_keys < kTreeTile && (!DUAL || wg == 0)) {
         // (the V tile may still be in flight: wait for it before writing)
         const int vst = i % G::kVStages;
-        if (!mbar_wait(&v_full[vst], (i / G::kVStages) & 1)) {
+        if (!mbar_wait(&v_full[vst], v_phase(i))) {
           softmax_ok = false;
           break;
         }

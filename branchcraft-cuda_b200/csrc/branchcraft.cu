@@ -130,7 +130,7 @@ bool encode_draft_map(CUtensorMap* map, const void* base, int dim, int heads, in
 // wrote them.
 cudaError_t launch_merge(int dim, int rows, int splits, const float* pml, const float* pa,
                          float* out, cudaStream_t stream, int per_block = 0,
-                         long long block_stride = 0) {
+                         long long block_stride = 0, float* out_ml = nullptr) {
   if (per_block <= 0) per_block = splits;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -141,10 +141,15 @@ cudaError_t launch_merge(int dim, int rows, int splits, const float* pml, const 
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (out_ml)  // merged state, not the normalised rows
+    return dim == 64 ? cudaLaunchKernelEx(&cfg, merge_kernel<64, true>, rows, splits, per_block,
+                                          block_stride, pml, pa, out, out_ml)
+                     : cudaLaunchKernelEx(&cfg, merge_kernel<128, true>, rows, splits, per_block,
+                                          block_stride, pml, pa, out, out_ml);
   return dim == 64 ? cudaLaunchKernelEx(&cfg, merge_kernel<64>, rows, splits, per_block,
-                                        block_stride, pml, pa, out)
+                                        block_stride, pml, pa, out, out_ml)
                    : cudaLaunchKernelEx(&cfg, merge_kernel<128>, rows, splits, per_block,
-                                        block_stride, pml, pa, out);
+                                        block_stride, pml, pa, out, out_ml);
 }
 
 template <int D, int RT, bool OUT_HALF>
@@ -389,13 +394,29 @@ cudaError_t launch_tree_t(TreeParams& p, const CUtensorMap* maps, int items, int
 // (R = 128 / (nodes * group)); a group whose page tables match shares each
 // K/V tile of the prefix. FP32 output accumulates P as FP16 hi + lo (FP32-exact
 // products); FP16 output uses one FP16 P, matching its own rounding.
+// The batch commit fused into a tree launch (bc_tree_verify_commit).
+struct FusedCommit {
+  const int *clone_src, *clone_dst, *entry_request, *entry_node, *entry_page, *entry_slot;
+  int nclones, nentries;
+};
+
 cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix_k,
                       const void* prefix_v, const int* pages, const int* lengths,
                       const void* draft_k, const void* draft_v, const int* parent, void* out,
-                      bool out_half, int nodes, cudaStream_t stream) {
+                      bool out_half, int nodes, cudaStream_t stream,
+                      const FusedCommit* commit = nullptr) {
   if (!basic_shape_ok(s) || nodes < 1 || nodes > BC_MAX_NODES || !prefix_k || !prefix_v ||
       !pages || !lengths || !draft_q || !draft_k || !draft_v || !parent || !out)
     return cudaErrorInvalidValue;
+  if (commit) {
+    const FusedCommit& c = *commit;
+    if (c.nclones < 0 || c.nclones > 256 || c.nentries < 0 ||
+        (c.nclones > 0 && (!c.clone_src || !c.clone_dst)) ||
+        (c.nentries > 0 && (!c.entry_request || !c.entry_node || !c.entry_page || !c.entry_slot)) ||
+        ((reinterpret_cast<uintptr_t>(prefix_k) | reinterpret_cast<uintptr_t>(prefix_v) |
+          reinterpret_cast<uintptr_t>(draft_k) | reinterpret_cast<uintptr_t>(draft_v)) % 16))
+      return cudaErrorInvalidValue;
+  }
   if ((reinterpret_cast<uintptr_t>(draft_q) | reinterpret_cast<uintptr_t>(out)) % 16)
     return cudaErrorInvalidValue;
   const int dev = current_device();
@@ -438,6 +459,21 @@ cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix
   p.out = out;
   p.scale_log2 = kLog2e / std::sqrt(float(s->dim));
   p.err = err;
+  if (commit) {
+    p.nclones = commit->nclones;
+    p.nentries = commit->nentries;
+    p.commit_tasks = 8 * commit->nclones + commit->nentries;
+    p.cache_k = static_cast<__half*>(const_cast<void*>(prefix_k));
+    p.cache_v = static_cast<__half*>(const_cast<void*>(prefix_v));
+    p.draft_k = static_cast<const __half*>(draft_k);
+    p.draft_v = static_cast<const __half*>(draft_v);
+    p.clone_src = commit->clone_src;
+    p.clone_dst = commit->clone_dst;
+    p.entry_request = commit->entry_request;
+    p.entry_node = commit->entry_node;
+    p.entry_page = commit->entry_page;
+    p.entry_slot = commit->entry_slot;
+  }
   CUtensorMap maps[4];
   bool sm = false;
   const long long hs = s->dim, ss = (long long)s->kv_heads * s->dim, bs = 16 * ss;
@@ -551,6 +587,19 @@ int bc_tree_verify_f16(const bc_shape* s, const void* draft_q, const void* prefi
                        void* output_f16, int nodes, void* stream) {
   return tree_core(s, draft_q, prefix_k, prefix_v, pages, lengths, draft_k, draft_v, parent,
                    output_f16, true, nodes, static_cast<cudaStream_t>(stream));
+}
+
+int bc_tree_verify_commit(const bc_shape* s, const void* draft_q, void* cache_k, void* cache_v,
+                          const int* pages, const int* lengths, const void* draft_k,
+                          const void* draft_v, const int* parent, void* output, int output_f16,
+                          int nodes, const int* clone_src, const int* clone_dst, int nclones,
+                          const int* entry_request, const int* entry_node,
+                          const int* entry_page, const int* entry_slot, int nentries,
+                          void* stream) {
+  const FusedCommit c{clone_src, clone_dst, entry_request, entry_node, entry_page, entry_slot,
+                      nclones, nentries};
+  return tree_core(s, draft_q, cache_k, cache_v, pages, lengths, draft_k, draft_v, parent,
+                   output, output_f16 != 0, nodes, static_cast<cudaStream_t>(stream), &c);
 }
 
 int bc_packed_decode_kv(const bc_shape* s, const void* q, const void* packed_kv,
@@ -681,6 +730,15 @@ int bc_merge_partials(int splits, int rows, int dim, const float* partial_ml,
     return cudaErrorInvalidValue;
   return launch_merge(dim, rows, splits, partial_ml, partial_a, out,
                       static_cast<cudaStream_t>(stream));
+}
+
+int bc_merge_to_partial(int splits, int rows, int dim, const float* partial_ml,
+                        const float* partial_a, float* out_ml, float* out_a, void* stream) {
+  if (splits < 1 || rows < 1 || (dim != 64 && dim != 128) || !partial_ml || !partial_a ||
+      !out_ml || !out_a)
+    return cudaErrorInvalidValue;
+  return launch_merge(dim, rows, splits, partial_ml, partial_a, out_a,
+                      static_cast<cudaStream_t>(stream), 0, 0, out_ml);
 }
 
 int bc_merge_gathered(int world, int splits, int rows, int dim, const float* gathered,

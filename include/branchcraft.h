@@ -128,6 +128,26 @@ int bc_commit_batch(const bc_shape* shape, int nodes, const void* draft_k,
                     const int* entry_node, const int* entry_page, const int* entry_slot,
                     int nentries, void* stream);
 
+/* One speculative-verification step in ONE launch: bc_tree_verify (FP32
+ * output, or FP16 with output_f16 != 0) over cache_k / cache_v, and the batch
+ * copy-on-write commit of bc_commit_batch (same arrays and semantics, at most
+ * 256 clones) into the same cache. The commit runs concurrently with the
+ * verification, so the call requires what a copy-on-write plan guarantees
+ * (bc_cow.PagePool, the reference's PagedTreeCache.commit,
+ * python/branchcraft_torch/transaction.py:114-150): the commit writes only
+ * fresh pages (clone destinations, pages no page table of this call holds)
+ * and, in place, slots at or past the length of every request whose table
+ * holds that page — bytes no verified row depends on. The verification then
+ * sees the cache as it was before the commit. Not in the reference (whose
+ * step is tree_verify, then per request a page copy and commit_path). */
+int bc_tree_verify_commit(const bc_shape* shape, const void* draft_q, void* cache_k,
+                          void* cache_v, const int* pages, const int* lengths,
+                          const void* draft_k, const void* draft_v, const int* parent,
+                          void* output, int output_f16, int nodes, const int* clone_src,
+                          const int* clone_dst, int nclones, const int* entry_request,
+                          const int* entry_node, const int* entry_page, const int* entry_slot,
+                          int nentries, void* stream);
+
 /* Decode straight from a packed cache with logical shape [P, Hkv, 16, 2D]:
  * K of (page, kv head, slot) starts at page*block_stride + head*head_stride +
  * slot*slot_stride elements and V at D elements after it; caller-supplied
@@ -158,6 +178,17 @@ int bc_packed_decode_kv(const bc_shape* shape, const void* q, const void* packed
  * (src/paged_gqa.cu:76-106); used after an all-gather of per-GPU partials. */
 int bc_merge_partials(int splits, int rows, int dim, const float* partial_ml,
                       const float* partial_a, float* out, void* stream);
+
+/* As bc_merge_partials, but storing the merged STATE instead of the
+ * normalised rows: out_ml[r*2 + {0,1}] = (M, L) and out_a[r*dim + d] the
+ * unnormalised accumulator, each partial weighted by exp(m_s - M) — one
+ * partial per row, in the layout the merge entry points read (rows whose m
+ * are all -inf give M = -inf, L = 0 and zeros). A GPU holding one shard of a
+ * context split reduces its many on-device splits to this one partial before
+ * the all-gather, so the exchange carries rows*(dim+2) floats per rank. Not
+ * in the reference; the math is its merge_kernel's (src/paged_gqa.cu:76-106). */
+int bc_merge_to_partial(int splits, int rows, int dim, const float* partial_ml,
+                        const float* partial_a, float* out_ml, float* out_a, void* stream);
 
 /* bc_merge_partials over partials gathered from `world` GPUs in ONE buffer:
  * gathered holds `world` blocks back to back, block r being rank r's

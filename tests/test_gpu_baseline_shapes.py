@@ -237,15 +237,19 @@ def test_config5b_one_gpu_decode(capi, million_context):
 
 
 @pytest.mark.parametrize("world", [2, 8])
-def test_config5b_split_across_emulated_ranks(capi, million_context, world):
+@pytest.mark.parametrize("reduce_local", [False, True])
+def test_config5b_split_across_emulated_ranks(capi, million_context, world, reduce_local):
     """The 1M-token context split into `world` contiguous page shards, one
-    bc_paged_decode_partial per shard into one partial buffer (37 unmerged
-    partials per q-head, as the bench runs it), the buffers stacked as the
-    all-gather delivers them and reduced by one bc_merge_gathered."""
+    bc_paged_decode_partial per shard (37 splits per q-head, as the bench runs
+    it). reduce_local: each shard's splits reduced to one partial per row by
+    bc_merge_to_partial (what a rank sends in the bench); otherwise all 37
+    are sent. The per-rank buffers are stacked as the all-gather delivers them
+    and reduced by one bc_merge_gathered."""
     from bc_dist import block_floats, block_views, shard_pages
 
     c = million_context
     splits = 37
+    sent = 1 if reduce_local else splits
     blocks = []
     capi.last_device_error()
     for r in range(world):
@@ -253,12 +257,18 @@ def test_config5b_split_across_emulated_ranks(capi, million_context, world):
         pages = c["pages"][:, shard.start:shard.stop].contiguous()
         length = torch.tensor([len(shard) * 16], device="cuda", dtype=torch.int32)
         s = capi.make_shape(1, HQ, HKV, D, len(shard), c["P"])
-        buf = torch.full((block_floats(splits, HQ, D),), float("nan"), device="cuda")
-        pml, pa = block_views(buf, splits, HQ, D)
+        part = torch.full((block_floats(splits, HQ, D),), float("nan"), device="cuda")
+        pml, pa = block_views(part, splits, HQ, D)
         capi.paged_decode_partial(s, c["q"], c["k"], c["v"], pages, length, pml, pa, splits)
-        blocks.append(buf)
+        if reduce_local:
+            buf = torch.full((block_floats(1, HQ, D),), float("nan"), device="cuda")
+            ml1, a1 = block_views(buf, 1, HQ, D)
+            capi.merge_to_partial(pml, pa, ml1[0], a1[0])
+            blocks.append(buf)
+        else:
+            blocks.append(part)
     out = torch.full((HQ, D), float("nan"), device="cuda")
-    capi.merge_gathered(torch.stack(blocks), world, splits, HQ, D, out)
+    capi.merge_gathered(torch.stack(blocks), world, sent, HQ, D, out)
     torch.cuda.synchronize()
     got = out.view(1, HQ, D).cpu().numpy()
     U.assert_close_baseline(got, c["expected"])

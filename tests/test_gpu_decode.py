@@ -102,3 +102,27 @@ def test_merge_partials_matches_oracle(capi):
     capi.merge_partials(torch.from_numpy(pml).cuda(), torch.from_numpy(pa).cuda(), out)
     torch.cuda.synchronize()
     assert U.max_abs(out.cpu().numpy(), expected) < 1e-5
+
+
+def test_merge_to_partial_then_merge_matches_oracle(capi):
+    """Reducing partials in two stages (two groups each merged to ONE partial
+    per row, then those merged) equals the oracle's one-stage merge; an
+    all-empty row stays zeros through both stages."""
+    rng = np.random.default_rng(19)
+    S, rows, D = 6, 10, 128
+    pml = rng.standard_normal((S, rows, 2)).astype(np.float32)
+    pml[..., 1] = np.abs(pml[..., 1]) + 0.1
+    pml[:, 4, 0] = -np.inf
+    pml[:3, 7, 0] = -np.inf  # empty in the whole first group
+    pa = rng.standard_normal((S, rows, D)).astype(np.float32)
+    expected = O.merge(pml, pa)
+    t_ml, t_a = torch.from_numpy(pml).cuda(), torch.from_numpy(pa).cuda()
+    st_ml = torch.empty(2, rows, 2, device="cuda")
+    st_a = torch.empty(2, rows, D, device="cuda")
+    for gi, sl in enumerate((slice(0, 3), slice(3, 6))):
+        capi.merge_to_partial(t_ml[sl].contiguous(), t_a[sl].contiguous(), st_ml[gi], st_a[gi])
+    out = torch.empty(rows, D, device="cuda")
+    capi.merge_partials(st_ml, st_a, out)
+    torch.cuda.synchronize()
+    assert U.max_abs(out.cpu().numpy(), expected) < 1e-5
+    assert np.isneginf(st_ml[0, 7, 0].item()) and st_ml[0, 7, 1].item() == 0.0

@@ -16,6 +16,15 @@ itself:
 * the data dependencies hold: S of a unit after its K tile landed and after
   the PV that last read its S/P buffer; P after S; PV after P and its V tile;
   a K or V stage refilled only after every unit that reads it is done.
+
+It also models the speculative first copies: each producer fills the first
+`spec_pre` stages of its ring (at most one pass) before the prologue knows the
+CTA's real key range. If the guess holds, those fills are the tiles of record;
+if not, it refills the same stages and every wait on one of those stages'
+full barriers looks one phase further. Either way the producers let the
+prologue end only once their speculative copies have landed: no consumer can
+then look at a speculated stage before its first phase is complete (a parity
+wait cannot tell the phase it wants from the one before that).
 """
 import random
 
@@ -37,24 +46,43 @@ class Barrier:
             self.pending = self.count
 
     def ready(self, wanted):
-        """Wait for completion number `wanted` (0-based) by its parity."""
+        """Wait for completion number `wanted` (0-based) by its parity, as the
+        hardware does: try_wait.parity(p) succeeds while the barrier's current
+        phase has the other parity. That is the right answer only within one
+        phase of the waiter; either side of that window is an error here."""
         if self.phase > wanted + 1:
             raise AssertionError(f"{self.name}: phase {self.phase} ran two ahead of a "
                                  f"waiter for completion {wanted} (parity aliasing)")
-        # try_wait.parity(p) succeeds once the phase of parity p has completed:
-        # with at most one phase of lead this is exactly phase > wanted.
-        return self.phase > wanted
+        if self.phase < wanted:
+            raise AssertionError(f"{self.name}: a waiter for completion {wanted} looked while "
+                                 f"the barrier was at phase {self.phase} (parity aliasing: "
+                                 f"the waiter is ahead)")
+        return (self.phase & 1) != (wanted & 1)
 
 
 def run_cta(ntiles, dual, seed, rescale_prob=0.1, zero_prob=0.2, s_bufs=S_BUFS,
-            p_per_group=False):
+            p_per_group=False, spec_pre=0, spec_ok=True, spec_gate=True):
     """One CTA's run; `s_bufs` and `p_per_group` (one "P written" barrier per
-    softmax group instead of per S/P buffer) model earlier designs."""
+    softmax group instead of per S/P buffer) model earlier designs;
+    `spec_pre` prefix tiles are copied speculatively, the guess holding or not
+    (`spec_ok`; when it holds the guessed range is the real one); without
+    `spec_gate` the prologue ends without waiting for those copies (the first,
+    faulty version of the speculation)."""
     S_BUFS = s_bufs  # noqa: N806  (shadows the kernel's constant)
     rng = random.Random(seed)
     rt = 2 if dual else 1
     ks = K_STAGES - 1 if dual else K_STAGES
     vs = V_STAGES - 1 if dual else V_STAGES
+    if spec_ok:
+        assert spec_pre <= ntiles
+    nspec_k, nspec_v = min(spec_pre, ks), min(spec_pre, vs)
+    xk, xv = (0, 0) if spec_ok else (nspec_k, nspec_v)
+
+    def k_done(i):  # completion index of k_full for tile i (the kernel's k_phase)
+        return i // ks + (1 if i % ks < xk else 0)
+
+    def v_done(i):
+        return i // vs + (1 if i % vs < xv else 0)
     nunits = ntiles * rt
     k_full = [Barrier(f"k_full{s}") for s in range(ks)]
     k_empty = [Barrier(f"k_empty{s}") for s in range(ks)]
@@ -85,34 +113,54 @@ def run_cta(ntiles, dual, seed, rescale_prob=0.1, zero_prob=0.2, s_bufs=S_BUFS,
     def tile_of(u):
         return (u >> 1, u & 1) if dual else (u, 0)
 
-    def k_producer(parity):
-        for i in range(parity, ntiles, 2):
-            st = i % ks
-            if i >= ks:
-                while not k_empty[st].ready(i // ks - 1):
+    def producer(parity, kind, full, empty, nst, nspec):
+        spec = list(range(parity, nspec, 2))
+        for i in spec:  # before the prologue knows the real range: stage i
+            log.append((f"{kind}_issue" if spec_ok else f"{kind}_spec_issue", i))
+            land = f"{kind}_land" if spec_ok else f"{kind}_spec_land"
+            later(f"tma{len(log)}", lambda i=i, land=land: (log.append((land, i)),
+                                                             full[i].arrive()), kind)
+            yield
+        if spec_gate or not spec_ok:  # the speculative copies land before the prologue ends
+            for i in spec:          # (ungated, only a failed guess waited, before refilling)
+                while not full[i].ready(0):
                     yield
-            log.append(("k_issue", i))
-            later(f"tma{len(log)}", lambda st=st, i=i: (log.append(("k_land", i)), k_full[st].arrive()),
-                  "k")
+        landed[f"{kind}{parity}"] = True
+        yield from prologue_barrier()
+        for i in range(parity, ntiles, 2):
+            if spec_ok and i < nspec:
+                continue
+            st = i % nst
+            if i >= nst:
+                while not empty[st].ready(i // nst - 1):
+                    yield
+            log.append((f"{kind}_issue", i))
+            later(f"tma{len(log)}", lambda st=st, i=i: (log.append((f"{kind}_land", i)),
+                                                         full[st].arrive()), kind)
             yield
 
+    def k_producer(parity):
+        return producer(parity, "k", k_full, k_empty, ks, nspec_k)
+
     def v_producer(parity):
-        for i in range(parity, ntiles, 2):
-            st = i % vs
-            if i >= vs:
-                while not v_empty[st].ready(i // vs - 1):
-                    yield
-            log.append(("v_issue", i))
-            later(f"tma{len(log)}", lambda st=st, i=i: (log.append(("v_land", i)), v_full[st].arrive()),
-                  "v")
+        return producer(parity, "v", v_full, v_empty, vs, nspec_v)
+
+    landed = {"k0": False, "k1": False, "v0": False, "v1": False}
+
+    def prologue_barrier():
+        """The CTA barrier that ends the prologue: the producers pass it only
+        once their speculative copies have landed, so every consumer starts
+        with each speculated stage's first phase complete."""
+        while spec_gate and not all(landed.values()):
             yield
 
     def s_issuer():
+        yield from prologue_barrier()
         for u in range(nunits):
             i, g = tile_of(u)
             kst, sb = i % ks, u % S_BUFS
             while not ((u < S_BUFS or s_free[sb].ready((u - S_BUFS) // S_BUFS)) and
-                       (g != 0 or k_full[kst].ready(i // ks))):
+                       (g != 0 or k_full[kst].ready(k_done(i)))):
                 yield
             log.append(("s_issue", u))
 
@@ -125,6 +173,7 @@ def run_cta(ntiles, dual, seed, rescale_prob=0.1, zero_prob=0.2, s_bufs=S_BUFS,
             yield
 
     def softmax(wg):
+        yield from prologue_barrier()
         i0, di = (0, 1) if dual else (wg, 2)
         for i in range(i0, ntiles, di):
             buf = wg if dual else (i & 1)
@@ -135,7 +184,7 @@ def run_cta(ntiles, dual, seed, rescale_prob=0.1, zero_prob=0.2, s_bufs=S_BUFS,
             log.append(("p_start", u))
             yield
             if rng.random() < zero_prob and (not dual or wg == 0):
-                while not v_full[i % vs].ready(i // vs):  # zeroing V rows
+                while not v_full[i % vs].ready(v_done(i)):  # zeroing V rows
                     yield
             if rng.random() < rescale_prob and i >= i0 + di:
                 while not pv_done[buf].ready((i - i0 - di) // di):  # O rescale
@@ -145,12 +194,13 @@ def run_cta(ntiles, dual, seed, rescale_prob=0.1, zero_prob=0.2, s_bufs=S_BUFS,
             yield
 
     def pv_issuer():
+        yield from prologue_barrier()
         for u in range(nunits):
             i, g = tile_of(u)
             vst, sb = i % vs, u % S_BUFS
             buf = g if dual else (i & 1)
             pb, pn = p_bar(u, buf)
-            while not (pb.ready(pn) and (g != 0 or v_full[vst].ready(i // vs))):
+            while not (pb.ready(pn) and (g != 0 or v_full[vst].ready(v_done(i)))):
                 yield
             log.append(("pv_issue", u))
 
@@ -186,11 +236,15 @@ def run_cta(ntiles, dual, seed, rescale_prob=0.1, zero_prob=0.2, s_bufs=S_BUFS,
     return log
 
 
-def check_order(log, ntiles, dual):
+def check_order(log, ntiles, dual, spec_pre=0, spec_ok=True):
     rt = 2 if dual else 1
     ks = K_STAGES - 1 if dual else K_STAGES
     vs = V_STAGES - 1 if dual else V_STAGES
     at = {ev: n for n, ev in enumerate(log)}
+    if not spec_ok:  # a stage's speculative copy landed before its refill
+        for kind, nst in (("k", ks), ("v", vs)):
+            for i in range(min(spec_pre, nst)):
+                assert at[(f"{kind}_spec_land", i)] < at.get((f"{kind}_issue", i), len(log))
     for u in range(ntiles * rt):
         i = u // rt
         assert at[("k_land", i)] < at[("s_issue", u)]
@@ -232,6 +286,35 @@ def test_model_finds_the_per_group_p_barrier_stall():
     for seed in range(40):
         try:
             run_cta(17, False, seed, s_bufs=3, p_per_group=True)
+        except AssertionError as e:
+            assert "parity aliasing" in str(e)
+            hits += 1
+    assert hits > 0
+
+
+@pytest.mark.parametrize("dual", [False, True])
+@pytest.mark.parametrize("ntiles,spec_pre,spec_ok", [
+    (1, 1, True), (3, 3, True), (5, 5, True), (6, 5, True), (17, 5, True), (4, 2, True),
+    (1, 5, False), (3, 5, False), (6, 5, False), (17, 3, False), (2, 1, False), (0, 4, False),
+])
+def test_speculative_first_copies(ntiles, spec_pre, spec_ok, dual):
+    """Speculative first copies, the guess holding (they are the tiles of
+    record) or failing (landed, refilled, waited for one phase further):
+    no aliasing, no deadlock, every dependency in order."""
+    for seed in range(12):
+        log = run_cta(ntiles, dual, seed * 104729 + ntiles, spec_pre=spec_pre, spec_ok=spec_ok)
+        check_order(log, ntiles, dual, spec_pre, spec_ok)
+
+
+def test_model_finds_the_ungated_speculation():
+    """Ending the prologue before the speculative copies land lets a consumer
+    of a failed guess wait for a stage's second phase while its first is
+    still pending (a parity wait then succeeds at once, on the wrong data) —
+    what the first version of the speculation did on the GPU."""
+    hits = 0
+    for seed in range(40):
+        try:
+            run_cta(3, False, seed, spec_pre=5, spec_ok=False, spec_gate=False)
         except AssertionError as e:
             assert "parity aliasing" in str(e)
             hits += 1
