@@ -30,7 +30,7 @@ EXPORTS = (
     "bc_tree_verify", "bc_tree_verify_f16", "bc_commit_path", "bc_commit_batch",
     "bc_packed_decode", "bc_packed_decode_kv", "bc_merge_partials",
     "bc_last_device_error", "bc_version", "bc_decode_static_scratch", "bc_merge_gathered",
-    "bc_merge_to_partial", "bc_tree_verify_commit",
+    "bc_merge_to_partial", "bc_tree_verify_commit", "bc_selftest_bounded_wait",
 )
 
 
@@ -66,6 +66,7 @@ _sigs = {
     "bc_merge_gathered": [_i, _i, _i, _i, _vp, _vp, _vp],
     "bc_merge_to_partial": [_i, _i, _i, _vp, _vp, _vp, _vp, _vp],
     "bc_decode_static_scratch": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp],
+    "bc_selftest_bounded_wait": [_i, _i, ctypes.c_uint, _vp],
     "bc_last_device_error": [_i],
     "bc_version": [],
 }
@@ -223,6 +224,11 @@ def decode_static_scratch(shape: Shape, q, k, v, pages, lengths, output, splits=
     if check:
         _check(rc, "bc_decode_static_scratch")
     return rc
+
+
+def selftest_bounded_wait(ctas, smem_bytes, limit_us, stream=None):
+    _check(_lib.bc_selftest_bounded_wait(ctas, smem_bytes, limit_us, _stream(stream)),
+           "bc_selftest_bounded_wait")
 
 
 def last_device_error(reset: bool = True) -> int:

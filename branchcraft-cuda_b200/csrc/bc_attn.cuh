@@ -60,6 +60,7 @@ struct AttnParams {
   float* partial_ml;
   float scale_log2;  // softmax scale * log2(e)
   unsigned* err;
+  unsigned token;    // this launch's abort token (s_launch_token)
 };
 
 template <int D>
@@ -113,6 +114,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // Barriers need no input: set them up before waiting for the preceding
   // kernel (a programmatic dependent launch may start while it finishes).
   if (threadIdx.x == 0) {
+    s_launch_token = p.token;  // (read by the bounded waits, after the set-up barrier)
 #pragma unroll
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);

@@ -21,6 +21,15 @@ enum DeviceError : unsigned {
 // A bounded wait gives up after this many nanoseconds of %globaltimer.
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 
+// Launch-scoped abort: every launch carries a token (unique per process,
+// never 0) that its kernels copy into s_launch_token at entry. The first
+// bounded wait of a launch that gives up stores the launch's token here; every
+// other wait of the same launch, in any CTA and any wave, sees it at its next
+// check and gives up at once, so a systematic stall costs one wait limit, not
+// one per CTA wave. A later launch has another token and is unaffected.
+__device__ unsigned g_abort_token;
+__shared__ unsigned s_launch_token;
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -63,15 +72,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete; false after
-// kWaitLimitNs without completion.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// `limit_ns` without completion, or as soon as another wait of this launch
+// has given up (then the abort is already recorded).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = globaltimer_ns();
+  const unsigned token = s_launch_token;
   for (;;) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer_ns() - start > kWaitLimitNs) return false;
+    if (token != 0u && *reinterpret_cast<volatile unsigned*>(&g_abort_token) == token) return false;
+    if (globaltimer_ns() - start > limit_ns) {
+      if (token != 0u) atomicExch(&g_abort_token, token);
+      return false;
+    }
   }
 }
 

@@ -96,6 +96,7 @@ struct TreeParams {
   void* out;            // [B, N, Hq, D] FP32 or FP16
   float scale_log2;
   unsigned* err;
+  unsigned token;       // this launch's abort token (s_launch_token)
   // The batch copy-on-write commit fused into the launch (commit_tasks > 0):
   // its tasks (commit_batch_task) run on warps 12-15 once their own roles are
   // done, spread over the grid's CTAs. The commit writes only bytes no
@@ -226,6 +227,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   // (a programmatic dependent launch may start while that kernel finishes):
   // barriers, the TMEM allocation, the tensor-map prefetch.
   if (tid == 0) {
+    s_launch_token = p.token;  // (read by the bounded waits, after the set-up barrier)
     for (int s = 0; s < G::kKStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);

@@ -52,6 +52,14 @@ unsigned* error_word(int dev) {
   return p;
 }
 
+// A fresh abort token for each launch (never 0: 0 disables the abort check).
+unsigned next_launch_token() {
+  static std::atomic<unsigned> counter{0};
+  unsigned t = counter.fetch_add(1, std::memory_order_relaxed) + 1;
+  if (t == 0) t = counter.fetch_add(1, std::memory_order_relaxed) + 1;
+  return t;
+}
+
 int sm_count(int dev) {
   static std::atomic<int> cache[kMaxDevices];
   int n = cache[dev].load(std::memory_order_relaxed);
@@ -240,6 +248,7 @@ AttnParams base_params(const bc_shape* s, unsigned* err) {
   p.physical_pages = s->physical_pages;
   p.rows = p.group;
   p.err = err;
+  p.token = next_launch_token();
   return p;
 }
 
@@ -459,6 +468,7 @@ cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix
   p.out = out;
   p.scale_log2 = kLog2e / std::sqrt(float(s->dim));
   p.err = err;
+  p.token = next_launch_token();
   if (commit) {
     p.nclones = commit->nclones;
     p.nentries = commit->nentries;
@@ -498,6 +508,24 @@ cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix
                     : launch_tree_t<128, true, false, true>(p, maps, it, tiles, TreeGeom<128, true, true>::smem_bytes(anc_rows), stream);
   return out_half ? launch_tree_t<128, false, true, false>(p, maps, it, tiles, TreeGeom<128, false>::smem_bytes(anc_rows), stream)
                   : launch_tree_t<128, true, false, false>(p, maps, it, tiles, TreeGeom<128, true>::smem_bytes(anc_rows), stream);
+}
+
+// Self-test of the bounded waits: every CTA waits on an mbarrier that no
+// one arrives at, with a short limit. The first wait to give up records the
+// launch's abort token; the CTAs of later waves then give up at their first
+// check. `smem` bytes of dynamic shared memory per CTA control how many CTAs
+// share an SM (hence the waves).
+__global__ void __launch_bounds__(32) selftest_wait_kernel(unsigned long long limit_ns,
+                                                           unsigned token, unsigned* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    s_launch_token = token;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (!__all_sync(0xffffffffu, mbar_wait(&bar, 0, limit_ns)) && threadIdx.x == 0)
+    atomicOr(err, kErrTimeout);
 }
 
 }  // namespace
@@ -814,6 +842,22 @@ int bc_decode_static_scratch(const bc_shape* s, const void* q, const void* k, co
                            1.0f / std::sqrt(float(s->dim)), splits,
                            splits > 1 ? kSplitGlobal : kSplitNone, false, partial_a, partial_ml,
                            false, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int bc_selftest_bounded_wait(int ctas, int smem_bytes, unsigned limit_us, void* stream) {
+  if (ctas < 1 || smem_bytes < 0 || smem_bytes > 200 * 1024 || limit_us < 1 ||
+      limit_us > 2000000u)
+    return cudaErrorInvalidValue;
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  unsigned* err = error_word(dev);
+  if (!err) return cudaErrorInvalidDevice;
+  cudaError_t e = cudaFuncSetAttribute(selftest_wait_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e != cudaSuccess) return e;
+  selftest_wait_kernel<<<ctas, 32, size_t(smem_bytes), static_cast<cudaStream_t>(stream)>>>(
+      (unsigned long long)limit_us * 1000ull, next_launch_token(), err);
+  return cudaGetLastError();
 }
 
 unsigned bc_last_device_error(int reset) {

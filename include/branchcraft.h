@@ -233,6 +233,16 @@ int bc_decode_static_scratch(const bc_shape* shape, const void* q, const void* k
                              const void* v, const int* pages, const int* lengths,
                              float* output, int splits, void* stream);
 
+/* Self-test of the bounded waits every kernel here uses: `ctas` CTAs (with
+ * smem_bytes of dynamic shared memory each, up to 200 KB, which sets how many
+ * share an SM and so how many waves run) each wait on a barrier nothing
+ * completes, giving up after limit_us microseconds (at most 2 s) and setting
+ * BC_ERR_TIMEOUT. The first wait to give up aborts the launch: waits of later
+ * waves give up at their first check, so the launch takes about one limit,
+ * not one per wave. No fault, trap or unbounded spin is involved. Not in the
+ * reference. */
+int bc_selftest_bounded_wait(int ctas, int smem_bytes, unsigned limit_us, void* stream);
+
 /* Returns the current device's error word (BC_ERR_* bits; 0 = clean) after
  * synchronising that device; reset != 0 clears it. */
 unsigned bc_last_device_error(int reset);

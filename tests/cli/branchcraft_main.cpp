@@ -16,6 +16,8 @@
 #include <fstream>
 #include <iomanip>
 #include <iostream>
+#include <iterator>
+#include <numeric>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -200,14 +202,16 @@ struct TreeGpu {
   }
 };
 
+// The comparison the CLI gates on: the largest elementwise |a - b|, where a
+// pair with a non-finite member counts as an infinite difference (so a NaN or
+// an overflow can never pass a tolerance).
 float max_abs_error(const std::vector<float>& a, const std::vector<float>& b) {
   if (a.size() != b.size()) throw std::runtime_error("comparison size mismatch");
-  float worst = 0;
-  for (size_t i = 0; i < a.size(); ++i) {
-    if (!std::isfinite(a[i]) || !std::isfinite(b[i])) return INFINITY;
-    worst = std::max(worst, std::fabs(a[i] - b[i]));
-  }
-  return worst;
+  const auto gap = [](float x, float y) {
+    return std::isfinite(x) && std::isfinite(y) ? std::fabs(x - y) : INFINITY;
+  };
+  const auto larger = [](float x, float y) { return x < y ? y : x; };
+  return std::transform_reduce(a.begin(), a.end(), b.begin(), 0.0f, larger, gap);
 }
 
 void check_device_errors() {
@@ -370,26 +374,39 @@ Fixture make_expanded_fixture(const TreeFixture& tree) {
   const size_t token_elems = size_t(ps.kv_heads) * ps.dim;
   flat.k.assign(size_t(flat.shape.physical_pages) * kPageSize * token_elems, 0);
   flat.v.assign(flat.k.size(), 0);
-  int next_page = 0;
+  // Sequences take consecutive physical pages in order; each token's K/V row
+  // comes either from the shared prefix (through the request's page table) or
+  // from the draft rows of its path node.
+  struct Source {
+    const std::vector<uint16_t>* k;
+    const std::vector<uint16_t>* v;
+    size_t row;  // element offset of the token's row
+  };
+  int page_cursor = 0;
   for (int seq = 0; seq < sequences; ++seq) {
     const int b = seq / tree.nodes;
-    for (int p = 0; p < (lengths[seq] + kPageSize - 1) / kPageSize; ++p)
-      flat.pages[size_t(seq) * max_pages + p] = next_page++;
-    for (int t = 0; t < lengths[seq]; ++t) {
-      const int dst_page = flat.pages[size_t(seq) * max_pages + t / kPageSize];
-      const size_t dst = (size_t(dst_page) * kPageSize + t % kPageSize) * token_elems;
-      const bool is_prefix = t < tree.prefix.lengths[b];
-      size_t src;
-      if (is_prefix) {
-        const int page = tree.prefix.pages[size_t(b) * ps.max_pages + t / kPageSize];
-        src = (size_t(page) * kPageSize + t % kPageSize) * token_elems;
-      } else {
-        src = (size_t(b) * tree.nodes + paths[seq][t - tree.prefix.lengths[b]]) * token_elems;
+    const int prefix_len = tree.prefix.lengths[b];
+    std::vector<Source> rows;
+    rows.reserve(lengths[seq]);
+    for (int t = 0; t < prefix_len; ++t) {
+      const int page = tree.prefix.pages[size_t(b) * ps.max_pages + t / kPageSize];
+      rows.push_back({&tree.prefix.k, &tree.prefix.v,
+                      (size_t(page) * kPageSize + t % kPageSize) * token_elems});
+    }
+    for (int node : paths[seq])
+      rows.push_back({&tree.draft_k, &tree.draft_v,
+                      (size_t(b) * tree.nodes + node) * token_elems});
+    int* table = flat.pages.data() + size_t(seq) * max_pages;
+    for (size_t first = 0; first < rows.size(); first += kPageSize) {
+      const int page = page_cursor++;
+      table[first / kPageSize] = page;
+      const size_t count = std::min<size_t>(kPageSize, rows.size() - first);
+      for (size_t slot = 0; slot < count; ++slot) {
+        const Source& src = rows[first + slot];
+        const size_t dst = (size_t(page) * kPageSize + slot) * token_elems;
+        std::copy_n(src.k->begin() + src.row, token_elems, flat.k.begin() + dst);
+        std::copy_n(src.v->begin() + src.row, token_elems, flat.v.begin() + dst);
       }
-      const auto& k = is_prefix ? tree.prefix.k : tree.draft_k;
-      const auto& v = is_prefix ? tree.prefix.v : tree.draft_v;
-      std::copy_n(k.begin() + src, token_elems, flat.k.begin() + dst);
-      std::copy_n(v.begin() + src, token_elems, flat.v.begin() + dst);
     }
   }
   return flat;
@@ -496,33 +513,57 @@ void run_bench(const std::string& output_path, bool quick) {
   std::cout << "Wrote " << output_path << '\n';
 }
 
-int main(int argc, char** argv) {
-  try {
-    if (argc < 2) {
-      std::cerr << "Usage: branchcraft test | bench | tree-bench [--quick] [--output FILE]\n";
-      return 2;
+namespace {
+
+// Options of the bench modes: `--quick` and `--output FILE`, in any order.
+struct BenchOptions {
+  bool quick = false;
+  std::string output;
+};
+
+BenchOptions parse_bench_options(const std::vector<std::string>& args, std::string output) {
+  BenchOptions opt;
+  opt.output = std::move(output);
+  for (auto it = args.begin(); it != args.end(); ++it) {
+    if (*it == "--quick") {
+      opt.quick = true;
+    } else if (*it == "--output" && std::next(it) != args.end()) {
+      opt.output = *++it;
+    } else {
+      throw std::runtime_error("unknown or incomplete argument: " + *it);
     }
-    const std::string mode = argv[1];
-    if (mode == "test") {
+  }
+  return opt;
+}
+
+}  // namespace
+
+// The reference's command line (src/main.cu:527-553): `test`, `bench` and
+// `tree-bench`, exit code 2 with the usage line when no mode is given, 1 on
+// any failure.
+int main(int argc, char** argv) {
+  const std::vector<std::string> args(argv + std::min(argc, 1), argv + argc);
+  if (args.empty()) {
+    std::cerr << "Usage: branchcraft test | bench | tree-bench [--quick] [--output FILE]\n";
+    return 2;
+  }
+  const std::vector<std::string> rest(args.begin() + 1, args.end());
+  try {
+    if (args[0] == "test") {
       run_tests();
       run_tree_tests();
-    } else if (mode == "bench" || mode == "tree-bench") {
-      bool quick = false;
-      std::string output = mode == "bench" ? "decode_results.csv" : "tree_results.csv";
-      for (int i = 2; i < argc; ++i) {
-        const std::string arg = argv[i];
-        if (arg == "--quick") quick = true;
-        else if (arg == "--output" && i + 1 < argc) output = argv[++i];
-        else throw std::runtime_error("unknown or incomplete argument: " + arg);
-      }
-      if (mode == "bench") run_bench(output, quick);
-      else run_tree_bench(output, quick);
+    } else if (args[0] == "bench") {
+      const BenchOptions opt = parse_bench_options(rest, "decode_results.csv");
+      run_bench(opt.output, opt.quick);
+    } else if (args[0] == "tree-bench") {
+      const BenchOptions opt = parse_bench_options(rest, "tree_results.csv");
+      run_tree_bench(opt.output, opt.quick);
     } else {
-      throw std::runtime_error("unknown mode: " + mode);
+      throw std::runtime_error("unknown mode: " + args[0]);
     }
-    return 0;
   } catch (const std::exception& e) {
     std::cerr << "ERROR: " << e.what() << '\n';
     return 1;
   }
+  return 0;
 }
