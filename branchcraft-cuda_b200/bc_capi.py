@@ -31,6 +31,7 @@ EXPORTS = (
     "bc_packed_decode", "bc_packed_decode_kv", "bc_merge_partials",
     "bc_last_device_error", "bc_version", "bc_decode_static_scratch", "bc_merge_gathered",
     "bc_merge_to_partial", "bc_tree_verify_commit", "bc_selftest_bounded_wait",
+    "bc_cow_plan", "bc_tree_step",
 )
 
 
@@ -67,6 +68,10 @@ _sigs = {
     "bc_merge_to_partial": [_i, _i, _i, _vp, _vp, _vp, _vp, _vp],
     "bc_decode_static_scratch": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "bc_selftest_bounded_wait": [_i, _i, ctypes.c_uint, _vp],
+    "bc_cow_plan": [_i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp,
+                    _vp, _vp, _vp, _vp, _vp, _vp],
+    "bc_tree_step": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp,
+                     _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "bc_last_device_error": [_i],
     "bc_version": [],
 }
@@ -174,6 +179,54 @@ def tree_verify_commit(shape, draft_q, cache_k, cache_v, pages, lengths, draft_k
         1 if output.dtype == torch.float16 else 0, nodes, _ptr(clone_src), _ptr(clone_dst),
         nclones, _ptr(entry_request), _ptr(entry_node), _ptr(entry_page), _ptr(entry_slot),
         nentries, _stream(stream)), "bc_tree_verify_commit")
+
+
+class CowPlan:
+    """Device buffers of one batch's commit plan (capacities: `batch` clones,
+    `batch * nodes` entries) and the page tables after the commit."""
+
+    def __init__(self, batch, nodes, max_pages_out, device="cuda"):
+        i32 = dict(device=device, dtype=torch.int32)
+        self.batch, self.nodes, self.max_pages_out = batch, nodes, max_pages_out
+        self.pages_out = torch.empty(batch, max_pages_out, **i32)
+        self.lengths_out = torch.empty(batch, **i32)
+        self.clone_src = torch.empty(batch, **i32)
+        self.clone_dst = torch.empty(batch, **i32)
+        self.entry_request = torch.empty(batch * nodes, **i32)
+        self.entry_node = torch.empty(batch * nodes, **i32)
+        self.entry_page = torch.empty(batch * nodes, **i32)
+        self.entry_slot = torch.empty(batch * nodes, **i32)
+        self.counts = torch.zeros(3, **i32)
+
+    def args(self):
+        return (_ptr(self.pages_out), self.max_pages_out, _ptr(self.lengths_out),
+                _ptr(self.clone_src), _ptr(self.clone_dst), _ptr(self.entry_request),
+                _ptr(self.entry_node), _ptr(self.entry_page), _ptr(self.entry_slot),
+                _ptr(self.counts))
+
+
+def cow_plan(pages, lengths, path_len, path_nodes, refcount, free_stack, free_count,
+             plan: CowPlan, physical_pages, stream=None):
+    """bc_cow_plan: the batch's copy-on-write bookkeeping on the device."""
+    batch, max_pages_in = pages.shape
+    (po, mpo, lo, cs, cd, er, en, ep, es, cnt) = plan.args()
+    _check(_lib.bc_cow_plan(batch, plan.nodes, physical_pages, _ptr(pages), max_pages_in,
+                            _ptr(lengths), _ptr(path_len), _ptr(path_nodes), _ptr(refcount),
+                            _ptr(free_stack), _ptr(free_count), po, mpo, lo, cs, cd, er, en,
+                            ep, es, cnt, _stream(stream)), "bc_cow_plan")
+
+
+def tree_step(shape, draft_q, cache_k, cache_v, pages, lengths, draft_k, draft_v, parent,
+              output, nodes, path_len, path_nodes, refcount, free_stack, free_count,
+              plan: CowPlan, stream=None):
+    """bc_tree_step: device planner, then verify + commit in one launch."""
+    (po, mpo, lo, cs, cd, er, en, ep, es, cnt) = plan.args()
+    _check(_lib.bc_tree_step(ctypes.byref(shape), _ptr(draft_q), _ptr(cache_k), _ptr(cache_v),
+                             _ptr(pages), _ptr(lengths), _ptr(draft_k), _ptr(draft_v),
+                             _ptr(parent), _ptr(output), 1 if output.dtype == torch.float16 else 0,
+                             nodes, _ptr(path_len), _ptr(path_nodes), _ptr(refcount),
+                             _ptr(free_stack), _ptr(free_count), po, mpo, lo, cs, cd, er, en, ep,
+                             es, cnt, _stream(stream)), "bc_tree_step")
 
 
 def packed_decode(shape, q, packed_kv, pages, lengths, output, block_stride, head_stride,

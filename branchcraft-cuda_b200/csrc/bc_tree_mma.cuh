@@ -104,6 +104,10 @@ struct TreeParams {
   // request's length: the copy-on-write plan's contract), so it needs no
   // ordering against the verification.
   int commit_tasks, nclones, nentries;
+  // (with a device-made plan: nclones / nentries are the plan arrays'
+  // capacities and plan_counts[0..2] = clones, entries, planner status; a
+  // nonzero status commits nothing)
+  const int* plan_counts;
   __half* cache_k;
   __half* cache_v;
   const __half* draft_k;
@@ -786,14 +790,21 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     // Warps 12-15 (both idle by now: the odd-tile producers have issued
     // their last copies, the ancestor sets are written) take the CTA's share
     // of the batch commit's tasks.
+    int nclones = p.nclones, nentries = p.nentries;
+    if (p.plan_counts) {  // a plan made on the device by the preceding launch
+      const bool ok = p.plan_counts[2] == 0;
+      nclones = ok ? min(max(p.plan_counts[0], 0), p.nclones) : 0;
+      nentries = ok ? min(max(p.plan_counts[1], 0), p.nentries) : 0;
+    }
     CommitScratch& sc = *reinterpret_cast<CommitScratch*>(smem + G::kCommitOff);
     const int ncta = int(gridDim.x * gridDim.z);
     const int row_halves = p.hkv * D;
-    for (int task = int(blockIdx.x + gridDim.x * blockIdx.z); task < p.commit_tasks; task += ncta)
+    const int tasks = 8 * nclones + nentries;
+    for (int task = int(blockIdx.x + gridDim.x * blockIdx.z); task < tasks; task += ncta)
       commit_batch_task<128>(task, tid - 384, [] { named_barrier_sync(4, 128); }, sc, row_halves,
                              p.batch, p.nodes, p.physical_pages, p.draft_k, p.draft_v, p.cache_k,
-                             p.cache_v, p.clone_src, p.clone_dst, p.nclones, p.entry_request,
-                             p.entry_node, p.entry_page, p.entry_slot, p.nentries, p.err);
+                             p.cache_v, p.clone_src, p.clone_dst, nclones, p.entry_request,
+                             p.entry_node, p.entry_page, p.entry_slot, nentries, p.err);
   }
   // ---- epilogue of warps 8-15: the barriers of the softmax warps' epilogue,
   // the TMEM release, and a share of the owners' sums.

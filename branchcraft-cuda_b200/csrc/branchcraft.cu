@@ -18,6 +18,7 @@
 
 #include "bc_attn.cuh"
 #include "bc_commit.cuh"
+#include "bc_cow_plan.cuh"
 #include "bc_tree_mma.cuh"
 #include "branchcraft.h"
 
@@ -406,7 +407,8 @@ cudaError_t launch_tree_t(TreeParams& p, const CUtensorMap* maps, int items, int
 // The batch commit fused into a tree launch (bc_tree_verify_commit).
 struct FusedCommit {
   const int *clone_src, *clone_dst, *entry_request, *entry_node, *entry_page, *entry_slot;
-  int nclones, nentries;
+  int nclones, nentries;         // counts, or the capacities of a device-made plan
+  const int* plan_counts;        // device-made plan: [clones, entries, status]
 };
 
 cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix_k,
@@ -473,6 +475,7 @@ cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix
     p.nclones = commit->nclones;
     p.nentries = commit->nentries;
     p.commit_tasks = 8 * commit->nclones + commit->nentries;
+    p.plan_counts = commit->plan_counts;
     p.cache_k = static_cast<__half*>(const_cast<void*>(prefix_k));
     p.cache_v = static_cast<__half*>(const_cast<void*>(prefix_v));
     p.draft_k = static_cast<const __half*>(draft_k);
@@ -625,7 +628,67 @@ int bc_tree_verify_commit(const bc_shape* s, const void* draft_q, void* cache_k,
                           const int* entry_page, const int* entry_slot, int nentries,
                           void* stream) {
   const FusedCommit c{clone_src, clone_dst, entry_request, entry_node, entry_page, entry_slot,
-                      nclones, nentries};
+                      nclones, nentries, nullptr};
+  return tree_core(s, draft_q, cache_k, cache_v, pages, lengths, draft_k, draft_v, parent,
+                   output, output_f16 != 0, nodes, static_cast<cudaStream_t>(stream), &c);
+}
+
+int bc_cow_plan(int batch, int nodes, int physical_pages, const int* pages_in,
+                int max_pages_in, const int* lengths_in, const int* path_len,
+                const int* path_nodes, int* refcount, int* free_stack, int* free_count,
+                int* pages_out, int max_pages_out, int* lengths_out, int* clone_src,
+                int* clone_dst, int* entry_request, int* entry_node, int* entry_page,
+                int* entry_slot, int* counts, void* stream) {
+  if (batch < 1 || nodes < 1 || nodes > BC_MAX_NODES || physical_pages < 1 ||
+      physical_pages > kCowPlanMaxPages || max_pages_in < 1 || max_pages_out < 1 ||
+      !pages_in || !lengths_in || !path_len || !path_nodes || !refcount || !free_stack ||
+      !free_count || !pages_out || !lengths_out || !clone_src || !clone_dst || !entry_request ||
+      !entry_node || !entry_page || !entry_slot || !counts ||
+      (long long)batch * nodes > 0x7fffffffLL || (long long)batch * max_pages_out > 0x7fffffffLL)
+    return cudaErrorInvalidValue;
+  const size_t smem = size_t(2) * physical_pages * sizeof(int);
+  static std::atomic<uint64_t> configured{0};
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  if (!(configured.load(std::memory_order_relaxed) & (uint64_t(1) << dev))) {
+    const cudaError_t e = cudaFuncSetAttribute(cow_plan_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               int(size_t(2) * kCowPlanMaxPages * sizeof(int)));
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(uint64_t(1) << dev);
+  }
+  CowPlanParams p{batch, nodes, physical_pages, max_pages_in, max_pages_out, pages_in,
+                  lengths_in, path_len, path_nodes, refcount, free_stack, free_count, pages_out,
+                  lengths_out, clone_src, clone_dst, entry_request, entry_node, entry_page,
+                  entry_slot, counts};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(kCowPlanThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, cow_plan_kernel, p);
+}
+
+int bc_tree_step(const bc_shape* s, const void* draft_q, void* cache_k, void* cache_v,
+                 const int* pages, const int* lengths, const void* draft_k, const void* draft_v,
+                 const int* parent, void* output, int output_f16, int nodes, const int* path_len,
+                 const int* path_nodes, int* refcount, int* free_stack, int* free_count,
+                 int* pages_out, int max_pages_out, int* lengths_out, int* clone_src,
+                 int* clone_dst, int* entry_request, int* entry_node, int* entry_page,
+                 int* entry_slot, int* counts, void* stream) {
+  if (!basic_shape_ok(s) || s->batch > 256) return cudaErrorInvalidValue;
+  int e = bc_cow_plan(s->batch, nodes, s->physical_pages, pages, s->max_pages, lengths, path_len,
+                      path_nodes, refcount, free_stack, free_count, pages_out, max_pages_out,
+                      lengths_out, clone_src, clone_dst, entry_request, entry_node, entry_page,
+                      entry_slot, counts, stream);
+  if (e != cudaSuccess) return e;
+  const FusedCommit c{clone_src, clone_dst, entry_request, entry_node, entry_page, entry_slot,
+                      s->batch, s->batch * nodes, counts};
   return tree_core(s, draft_q, cache_k, cache_v, pages, lengths, draft_k, draft_v, parent,
                    output, output_f16 != 0, nodes, static_cast<cudaStream_t>(stream), &c);
 }

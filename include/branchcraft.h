@@ -148,6 +148,45 @@ int bc_tree_verify_commit(const bc_shape* shape, const void* draft_q, void* cach
                           const int* entry_node, const int* entry_page, const int* entry_slot,
                           int nentries, void* stream);
 
+/* The page bookkeeping of a batch of copy-on-write commits, on the device:
+ * the refcount / free-list / clone decisions of the reference's
+ * PagedTreeCache.commit (python/branchcraft_torch/transaction.py:114-150),
+ * request b committing path_nodes[b, 0 .. path_len[b]) in batch order.
+ * State, updated in place: refcount[P], free_stack[0 .. *free_count) (the
+ * free list; its last entry is popped first, released pages are pushed) and,
+ * per request, pages_in [batch, max_pages_in] / lengths_in [batch] (read).
+ * Writes the page tables after the commit (pages_out [batch, max_pages_out],
+ * -1 past each row's end; lengths_out), the plan — clone_src / clone_dst
+ * (capacity batch) and entry_request / entry_node / entry_page / entry_slot
+ * (capacity batch*nodes), in bc_commit_batch's format — and counts[0..2] =
+ * (clones, entries, status). status 0: planned; 1: a path empty, longer than
+ * `nodes` or with a node id out of range; 2: not enough free pages (the
+ * reference's RuntimeError); 3: a malformed table or length. On a nonzero
+ * status the state is left unchanged and the plan is empty. P at most 24,576
+ * pages (the state is staged in shared memory). One single-CTA launch. Not in
+ * the reference (whose bookkeeping is host Python). */
+int bc_cow_plan(int batch, int nodes, int physical_pages, const int* pages_in,
+                int max_pages_in, const int* lengths_in, const int* path_len,
+                const int* path_nodes, int* refcount, int* free_stack, int* free_count,
+                int* pages_out, int max_pages_out, int* lengths_out, int* clone_src,
+                int* clone_dst, int* entry_request, int* entry_node, int* entry_page,
+                int* entry_slot, int* counts, void* stream);
+
+/* A whole speculative-verification step with no host round trip: bc_cow_plan
+ * on the batch's accepted paths, then bc_tree_verify_commit executing that
+ * plan (read from the device; a nonzero planner status commits nothing) in the
+ * verify launch. Two launches, the second a programmatic dependent of the
+ * first. `pages` / `lengths` are the tables before the commit (what the
+ * verification reads); the tables after it go to pages_out / lengths_out.
+ * shape->batch at most 256. Not in the reference. */
+int bc_tree_step(const bc_shape* shape, const void* draft_q, void* cache_k, void* cache_v,
+                 const int* pages, const int* lengths, const void* draft_k, const void* draft_v,
+                 const int* parent, void* output, int output_f16, int nodes,
+                 const int* path_len, const int* path_nodes, int* refcount, int* free_stack,
+                 int* free_count, int* pages_out, int max_pages_out, int* lengths_out,
+                 int* clone_src, int* clone_dst, int* entry_request, int* entry_node,
+                 int* entry_page, int* entry_slot, int* counts, void* stream);
+
 /* Decode straight from a packed cache with logical shape [P, Hkv, 16, 2D]:
  * K of (page, kv head, slot) starts at page*block_stride + head*head_stride +
  * slot*slot_stride elements and V at D elements after it; caller-supplied

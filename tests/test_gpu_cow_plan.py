@@ -1,0 +1,184 @@
+"""The device copy-on-write planner (bc_cow_plan) against the host planner
+(bc_cow.PagePool.plan_commit_batch, itself pinned to the sequential oracle of
+the reference's PagedTreeCache in test_cow_planner.py): on random transaction
+histories the device produces the same clones, entries, page tables, lengths,
+refcounts and free list, bit for bit; failed batches (a bad path, too few
+free pages) leave the device state unchanged, as the reference's errors leave
+its pool; and bc_tree_step runs a whole config-2 step (plan, verification and
+commit) from device state with the sequential result."""
+import numpy as np
+import pytest
+import torch
+
+import bc_testutil as U
+import oracle as O
+from bc_cow import PagePool
+from cow_oracle import CowOracle
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def capi():
+    import bc_capi
+
+    return bc_capi
+
+
+def _i32(x):
+    return torch.tensor(np.asarray(x, np.int32), device="cuda")
+
+
+def _device_state(pool: PagePool):
+    return (_i32(pool.refcount), _i32(pool.free + [0] * (pool.physical_pages - len(pool.free))),
+            _i32([len(pool.free)]))
+
+
+def _batch_inputs(pool, reqs, paths, nodes, width):
+    pages = _i32(pool.page_table(reqs, width))
+    lengths = _i32([pool.lengths[r] for r in reqs])
+    plen = _i32([len(p) for p in paths])
+    pn = np.full((len(reqs), nodes), -1, np.int32)
+    for b, p in enumerate(paths):  # (a path longer than `nodes` is cut; its length stays)
+        pn[b, :min(len(p), nodes)] = p[:nodes]
+    return pages, lengths, plen, _i32(pn)
+
+
+def _run_device(capi, pool, reqs, paths, nodes, width_in, width_out):
+    rc, stack, nfree = _device_state(pool)
+    pages, lengths, plen, pn = _batch_inputs(pool, reqs, paths, nodes, width_in)
+    plan = capi.CowPlan(len(reqs), nodes, width_out)
+    capi.cow_plan(pages, lengths, plen, pn, rc, stack, nfree, plan, pool.physical_pages)
+    torch.cuda.synchronize()
+    return plan, rc, stack, nfree
+
+
+def _assert_matches(pool, plan_host, reqs, plan, rc, stack, nfree, width_out):
+    cnt = plan.counts.cpu().tolist()
+    assert cnt[2] == 0
+    ncl, nent = cnt[0], cnt[1]
+    assert plan.clone_src[:ncl].tolist() == plan_host.clone_src
+    assert plan.clone_dst[:ncl].tolist() == plan_host.clone_dst
+    assert plan.entry_request[:nent].tolist() == plan_host.entry_request
+    assert plan.entry_node[:nent].tolist() == plan_host.entry_node
+    assert plan.entry_page[:nent].tolist() == plan_host.entry_page
+    assert plan.entry_slot[:nent].tolist() == plan_host.entry_slot
+    assert plan.pages_out.tolist() == pool.page_table(reqs, width_out)
+    assert plan.lengths_out.tolist() == [pool.lengths[r] for r in reqs]
+    assert rc.tolist() == pool.refcount
+    n = int(nfree.item())
+    assert stack[:n].tolist() == pool.free
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_random_histories_match_host_planner(capi, seed):
+    """Random new / fork / checkpoint / rollback / accept histories; every
+    batch commit planned on the device from the host's state, then on the
+    host, and compared."""
+    rng = np.random.default_rng(seed)
+    P, N = 64, 7
+    pool = PagePool(P)
+    live, snaps, batches = [], [], 0
+    for _ in range(60):
+        op = rng.choice(["new", "fork", "snap", "batch", "batch", "rollback", "accept"])
+        if op == "new" or not live:
+            try:
+                live.append(pool.new(int(rng.integers(1, 40))))
+            except RuntimeError:
+                pass
+        elif op == "fork":
+            live.append(pool.fork(int(rng.choice(live))))
+        elif op == "snap":
+            snaps.append(pool.checkpoint(int(rng.choice(live))))
+        elif op == "batch":
+            reqs = [int(x) for x in rng.choice(live, size=min(len(live), 4), replace=False)]
+            paths = [list(int(n) for n in rng.choice(N, size=int(rng.integers(1, N + 1)),
+                                                       replace=False)) for _ in reqs]
+            width_in = max(1, max(len(pool.pages[r]) for r in reqs))
+            width_out = width_in + 2
+            plan, rc, stack, nfree = _run_device(capi, pool, reqs, paths, N, width_in, width_out)
+            before = (pool.refcount.copy(), pool.free.copy())
+            try:
+                host = pool.plan_commit_batch([(r, paths[i], i) for i, r in enumerate(reqs)], N)
+            except RuntimeError:
+                assert plan.counts[2].item() == 2  # exhausted, state unchanged
+                assert rc.tolist() == before[0]
+                assert stack[:int(nfree.item())].tolist() == before[1]
+                continue
+            _assert_matches(pool, host, reqs, plan, rc, stack, nfree, width_out)
+            batches += 1
+        elif op == "rollback" and snaps:
+            pool.rollback(snaps.pop(int(rng.integers(len(snaps)))))
+        elif op == "accept" and snaps:
+            pool.accept(snaps.pop(int(rng.integers(len(snaps)))))
+    assert batches > 0
+
+
+def test_bad_paths_change_nothing(capi):
+    pool = PagePool(8)
+    a = pool.new(20)
+    b = pool.fork(a)
+    for paths in ([[0], []], [[0, 9], [1]], [[0] * 8, [1]]):
+        plan, rc, stack, nfree = _run_device(capi, pool, [a, b], paths, 7, 2, 4)
+        assert plan.counts.tolist() == [0, 0, 1]
+        assert rc.tolist() == pool.refcount
+        assert stack[:int(nfree.item())].tolist() == pool.free
+
+
+def test_exhausted_pool_changes_nothing(capi):
+    pool = PagePool(5)
+    a = pool.new(20)            # pages 0, 1 (the second partial)
+    pool.fork(a)
+    c = pool.new(40)            # pages 2, 3, 4: nothing left
+    plan, rc, stack, nfree = _run_device(capi, pool, [c, a], [[0], [0]], 7, 3, 4)
+    assert plan.counts.tolist() == [0, 0, 2]  # a's clone needs a free page
+    assert rc.tolist() == pool.refcount and int(nfree.item()) == 0
+
+
+def test_config2_step_from_device_state(capi):
+    """BASELINE config 2 in one call: the device plans the 8 commits from the
+    pool state (7 clones, the 8th in place), verifies and commits; the
+    verification equals the unfused verify, the cache the sequential oracle's,
+    the new page tables and state the host planner's."""
+    from bc_workloads import TreeCowWorkload
+
+    wl = TreeCowWorkload(seed=2040)
+    pool = PagePool(wl.pool_pages)
+    reqs = [pool.new(wl.prefix)] + [pool.fork(0) for _ in range(wl.batch - 1)]
+    rc, stack, nfree = _device_state(pool)
+    k0, v0 = wl.initial_cache()
+    ck, cv = U.to_dev(k0), U.to_dev(v0)
+    s = capi.make_shape(*wl.shape())
+    t = {n: U.to_dev(getattr(wl, n)) for n in ("draft_q", "draft_k", "draft_v", "parent",
+                                               "pages", "lengths")}
+    plen = _i32([len(p) for p in wl.paths])
+    pn = np.full((wl.batch, wl.nodes), -1, np.int32)
+    for b, p in enumerate(wl.paths):
+        pn[b, :len(p)] = p
+    plan = capi.CowPlan(wl.batch, wl.nodes, wl.max_pages)
+    out = torch.full((wl.batch, wl.nodes, wl.hq, wl.dim), float("nan"), device="cuda")
+    capi.last_device_error()
+    capi.tree_step(s, t["draft_q"], ck, cv, t["pages"], t["lengths"], t["draft_k"], t["draft_v"],
+                   t["parent"], out, wl.nodes, plen, _i32(pn), rc, stack, nfree, plan)
+    torch.cuda.synchronize()
+    assert capi.last_device_error() == 0
+    assert plan.counts.tolist() == [7, sum(len(p) for p in wl.paths), 0]
+    ref = torch.empty_like(out)
+    capi.tree_verify(s, t["draft_q"], U.to_dev(k0), U.to_dev(v0), t["pages"], t["lengths"],
+                     t["draft_k"], t["draft_v"], t["parent"], ref, wl.nodes)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    expected = O.tree(wl.shape(), wl.nodes, wl.draft_q, k0, v0, wl.pages, wl.lengths,
+                      wl.draft_k, wl.draft_v, wl.parent)
+    U.assert_close_baseline(out.cpu().numpy(), expected)
+    host = pool.plan_commit_batch([(reqs[b], wl.paths[b], b) for b in range(wl.batch)], wl.nodes)
+    _assert_matches(pool, host, reqs, plan, rc, stack, nfree, wl.max_pages)
+    cow = CowOracle(wl.pool_pages, wl.hkv, wl.dim)
+    r0 = cow.new(wl.prefix_k, wl.prefix_v)
+    oreqs = [r0] + [cow.fork(r0) for _ in range(wl.batch - 1)]
+    for b in range(wl.batch):
+        cow.commit(oreqs[b], wl.paths[b], wl.draft_k[b], wl.draft_v[b])
+    assert np.array_equal(U.half_bits(ck), cow.k)
+    assert np.array_equal(U.half_bits(cv), cow.v)
+    assert plan.pages_out.tolist() == [cow.pages[r] + [-1] * (wl.max_pages - len(cow.pages[r]))
+                                       for r in oreqs]
