@@ -176,6 +176,27 @@ def dist_env():
             int(os.environ.get("LOCAL_RANK", "0")))
 
 
+
+def graph_kernel_nodes(g):
+    """Kernel nodes of a captured torch CUDA graph (kept: keep_graph=True)."""
+    from cuda.bindings import runtime as rt
+
+    graph = rt.cudaGraph_t(init_value=g.raw_cuda_graph())
+    err, _, n = rt.cudaGraphGetNodes(graph, 0)
+    if err != rt.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"cudaGraphGetNodes: {err}")
+    err, nodes, n = rt.cudaGraphGetNodes(graph, n)
+    if err != rt.cudaError_t.cudaSuccess:
+        raise RuntimeError(f"cudaGraphGetNodes: {err}")
+    count = 0
+    for node in nodes[:n]:
+        err, kind = rt.cudaGraphNodeGetType(node)
+        if err != rt.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"cudaGraphNodeGetType: {err}")
+        count += kind == rt.cudaGraphNodeType.cudaGraphNodeTypeKernel
+    return count
+
+
 def to_dev(torch, a, device):
     a = np.ascontiguousarray(a)
     if a.dtype == np.uint16:
@@ -306,9 +327,12 @@ class TreeCow(Workload):
     is far below L2, so the bench rotates over `copies` independent copies of
     all of it, more than twice the L2 size in total: each step touches data
     last used `copies` steps earlier (cold in L2) and no flush kernel runs
-    between steps. A step is ONE C-ABI call, bc_tree_verify_commit (the batch
-    commit fused into the verify launch); device steps are replayed from one
-    CUDA graph per copy holding that call."""
+    between steps. A step is ONE C-ABI call, bc_tree_step: the device planner
+    (the copy-on-write page bookkeeping of the batch) and the verify launch
+    that also executes the planned commit. Every step reads the same pool
+    state and writes the state after it to separate arrays (the bench replays
+    one transaction). Device steps are replayed from one CUDA graph per copy
+    holding that call."""
 
     name = "tree-cow"
     unit = "TB/s"
@@ -329,14 +353,20 @@ class TreeCow(Workload):
             "e_req": np.array(plan.entry_request, np.int32),
             "e_node": np.array(plan.entry_node, np.int32),
             "e_page": np.array(plan.entry_page, np.int32),
-            "e_slot": np.array(plan.entry_slot, np.int32)}
+            "e_slot": np.array(plan.entry_slot, np.int32),
+            "path_len": np.array([len(p) for p in wl.paths], np.int32),
+            "path_nodes": np.array([p + [-1] * (wl.nodes - len(p)) for p in wl.paths], np.int32)}
         self.out_shape = (wl.batch, wl.nodes, wl.hq, wl.dim)
         self.out_dtype = torch.float32
         self.nodes = wl.nodes
-        # One launch per step: bc_tree_verify_commit runs the batch commit
-        # (7 clones, 23 rows) on idle warps of the verify kernel.
+        # One C-ABI call per step, bc_tree_step: the device planner (page
+        # bookkeeping of the 8 commits) and the verify launch that also runs
+        # the planned commit (7 clones, 23 rows) on its idle warps. The plan
+        # is made by one extra cluster of the verify launch when the grid
+        # stays one wave, else by a planner launch before it; `prepare`
+        # counts the launches in the captured step.
         self.fused = len(plan.clone_src) <= 256
-        self.launches = 1 if self.fused else 3
+        self.launches = 2 if self.fused else 3
         self.step_bytes = wl.verify_bytes() + wl.commit_bytes(plan)
         self.kernel_bytes = self.step_bytes if self.fused else wl.verify_bytes()
         self.kernel = ("tree_mma_kernel (tree_verify + the fused COW commit)" if self.fused
@@ -357,6 +387,19 @@ class TreeCow(Workload):
                           for _ in range(self.copies)]
         self.rot = 0
         self._argv = {}
+        if getattr(self, "wl", None) is not None and hasattr(self.wl, "pool"):
+            # The page pool's device state before the step (refcounts, free
+            # stack, free count; 2 KB), which every step reads, and the state
+            # after it, which it writes (one per rotating copy): the bench
+            # replays one step, and each replay plans from the same state.
+            pool = self.wl.pool
+            P = pool.physical_pages
+            st = np.array(pool.refcount + pool.free + [0] * (P - len(pool.free)) +
+                          [len(pool.free)], np.int32)
+            self.state0 = torch.from_numpy(st).to(self.device)
+            self.states = [self.state0.clone() for _ in range(self.copies)]
+            self.plans = [self.C.CowPlan(self.wl.batch, self.wl.nodes, self.wl.max_pages,
+                                         self.device) for _ in range(self.copies)]
 
     def _next(self):
         c = self.rot
@@ -387,16 +430,33 @@ class TreeCow(Workload):
                       P(d["clone_src"]), P(d["clone_dst"]), int(d["clone_src"].numel()),
                       P(d["e_req"]), P(d["e_node"]), P(d["e_page"]), P(d["e_slot"]),
                       int(d["e_node"].numel()), st)
+            sv = None
+            if "path_len" in d and hasattr(self, "states"):
+                npool = self.wl.pool_pages
+                stt = self.states[c]
+                sv = (ctypes.byref(self.shape), P(d["draft_q"]), P(ck), P(cv), P(d["pages"]),
+                      P(d["lengths"]), P(d["draft_k"]), P(d["draft_v"]), P(d["parent"]),
+                      P(self.outs[c]), int(self.out_dtype == self.torch.float16), self.nodes,
+                      P(d["path_len"]), P(d["path_nodes"]), P(self.state0[:npool]),
+                      P(self.state0[npool:2 * npool]), P(self.state0[2 * npool:]),
+                      P(stt[:npool]), P(stt[npool:2 * npool]), P(stt[2 * npool:]),
+                      *self.plans[c].args(), st)
             fn = (C.lib().bc_tree_verify_f16 if self.out_dtype == self.torch.float16
                   else C.lib().bc_tree_verify)
-            self._argv[key] = (fn, tv, cb, fv)
+            self._argv[key] = (fn, tv, cb, fv, sv)
         return self._argv[key]
 
-    def launch(self, c, stream=None, verify_only=False):
-        """One step on copy c: the fused verify + commit call (one foreign
-        call, one launch), or bc_tree_verify then bc_commit_batch."""
-        fn, tv, cb, fv = self._args(c, stream or self.torch.cuda.current_stream())
-        if fv is not None and getattr(self, "fused", False) and not verify_only:
+    def launch(self, c, stream=None, verify_only=False, host_plan=False):
+        """One step on copy c: bc_tree_step (the device plan made from the
+        pool state before the step, the state after it written to copy c's
+        arrays, and the verify with the fused commit); with host_plan the
+        fused verify + commit of the plan made once on the host
+        (bc_tree_verify_commit); verify_only: bc_tree_verify alone."""
+        stream = stream or self.torch.cuda.current_stream()
+        fn, tv, cb, fv, sv = self._args(c, stream)
+        if sv is not None and not verify_only and not host_plan:
+            rc = self.C.lib().bc_tree_step(*sv)
+        elif fv is not None and getattr(self, "fused", False) and not verify_only:
             rc = self.C.lib().bc_tree_verify_commit(*fv)
         else:
             rc = fn(*tv)
@@ -407,16 +467,23 @@ class TreeCow(Workload):
 
     def prepare(self):
         """One CUDA graph per rotating copy, captured from the step's C-ABI
-        calls (the library's per-device caches are warm by now)."""
+        calls (the library's per-device caches are warm by now). The step's
+        launch count is read from the captured graphs: their kernel nodes."""
         torch = self.torch
         self.graphs = []
         cap = torch.cuda.Stream()
+        kernels = set()
         for c in range(self.copies):
-            g = torch.cuda.CUDAGraph()
+            g = torch.cuda.CUDAGraph(keep_graph=True)
             with torch.cuda.graph(g, stream=cap):
                 self.launch(c, cap)
+            kernels.add(graph_kernel_nodes(g))
+            g.instantiate()
             self.graphs.append(g)
         torch.cuda.synchronize()
+        if len(kernels) != 1:
+            raise RuntimeError(f"the rotating copies' step graphs differ: {sorted(kernels)}")
+        self.launches = kernels.pop()
         self.graphed = True
 
     def device_step(self):
@@ -427,8 +494,16 @@ class TreeCow(Workload):
             self.launch(c)
 
     def kernel_step(self):
-        # the step's one kernel (verify + fused commit), or the verify alone
-        self.launch(self._next(), verify_only=not getattr(self, "fused", False))
+        # the dominant kernel: verify with the fused commit (of the host-made
+        # plan: the planner is a separate launch), or the verify alone
+        self.launch(self._next(), verify_only=not getattr(self, "fused", False), host_plan=True)
+
+    def alt_steps(self):
+        """Other forms of the same step, timed beside the headline one."""
+        if not hasattr(self, "states"):
+            return {}
+        return {"plan made once on the host (bc_tree_verify_commit: one launch)":
+                lambda: self.launch(self._next(), host_plan=True)}
 
     def e2e_step(self):
         c = self._next()
@@ -504,7 +579,10 @@ class TreeCow(Workload):
                 "verify_bytes_per_launch": wl.verify_bytes(),
                 "verify_flops_per_launch": wl.verify_flops(),
                 "commit_clones": len(self.plan.clone_src),
-                "commit_rows": len(self.plan.entry_node)}
+                "commit_rows": len(self.plan.entry_node),
+                "step": ("bc_tree_step: device COW planner (pool state in -> out), verify "
+                         "launch executing the planned commit" if hasattr(self, "states")
+                         else "bc_tree_verify + bc_commit_batch")}
 
     def cpu_baseline(self):
         """The oracle port (OpenMP over rows) on one full step."""
@@ -1140,6 +1218,14 @@ class Harness:
         for _ in range(R):
             self.barrier()
             kern.append(region(torch, wl.kernel_step, steps, stream))
+        alts = wl.alt_steps() if hasattr(wl, "alt_steps") else {}
+        alt_ms = {}
+        for name, fn in alts.items():
+            ms = []
+            for _ in range(R):
+                self.barrier()
+                ms.append(region(torch, fn, steps, stream))
+            alt_ms[name] = ms
         for _ in range(R):
             self.barrier()
             if hasattr(wl, "e2e_region"):
@@ -1149,8 +1235,11 @@ class Harness:
         self.barrier()
         t1 = time.time()
         err = C.last_device_error()
-        allv = self.max_over_ranks(dev + kern + e2e + [float(err)])
+        alt_flat = [x for ms in alt_ms.values() for x in ms]
+        allv = self.max_over_ranks(dev + kern + e2e + alt_flat + [float(err)])
         dev, kern, e2e, err = allv[:R], allv[R:2 * R], allv[2 * R:3 * R], int(allv[-1])
+        alt_all = allv[3 * R:-1]
+        alt_ms = {name: alt_all[i * R:(i + 1) * R] for i, name in enumerate(alt_ms)}
         dev_ms, kern_ms, e2e_ms = (statistics.median(x) for x in (dev, kern, e2e))
         world = self.world
         value = wl.value(steps * world, dev_ms * 1e-3)
@@ -1188,9 +1277,14 @@ class Harness:
                     "mode": ("pipelined: next step's H2D and previous step's D2H overlap the "
                              "compute" if hasattr(wl, "e2e_region") else
                              "sequential: H2D, compute, D2H per step")},
-            "gpu_launches": R * steps * (2 * wl.launches + wl.kernel_launches),
+            "gpu_launches": R * steps * (2 * wl.launches + wl.kernel_launches + len(alt_ms)),
             "roofline": roof, "clocks": sampler.window(t0, t1), "device_error_word": err,
         }
+        if alt_ms:
+            out["alternative_steps"] = {
+                name: {"ms_per_step": round(statistics.median(ms) / steps, 6),
+                       "value": round(wl.value(steps * world, statistics.median(ms) * 1e-3), 6)}
+                for name, ms in alt_ms.items()}
         if with_cpu:
             cb = wl.cpu_baseline()
             cb["value"] = float(f"{cb['value']:.6g}")

@@ -68,10 +68,11 @@ _sigs = {
     "bc_merge_to_partial": [_i, _i, _i, _vp, _vp, _vp, _vp, _vp],
     "bc_decode_static_scratch": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "bc_selftest_bounded_wait": [_i, _i, ctypes.c_uint, _vp],
-    "bc_cow_plan": [_i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp,
-                    _vp, _vp, _vp, _vp, _vp, _vp],
+    "bc_cow_plan": [_i, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
+                    _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "bc_tree_step": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp,
-                     _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+                     _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                     _vp],
     "bc_last_device_error": [_i],
     "bc_version": [],
 }
@@ -196,7 +197,7 @@ class CowPlan:
         self.entry_node = torch.empty(batch * nodes, **i32)
         self.entry_page = torch.empty(batch * nodes, **i32)
         self.entry_slot = torch.empty(batch * nodes, **i32)
-        self.counts = torch.zeros(3, **i32)
+        self.counts = torch.zeros(4, **i32)  # clones, entries, status, publication tag
 
     def args(self):
         return (_ptr(self.pages_out), self.max_pages_out, _ptr(self.lengths_out),
@@ -205,28 +206,36 @@ class CowPlan:
                 _ptr(self.counts))
 
 
-def cow_plan(pages, lengths, path_len, path_nodes, refcount, free_stack, free_count,
-             plan: CowPlan, physical_pages, stream=None):
-    """bc_cow_plan: the batch's copy-on-write bookkeeping on the device."""
+def _state(state_in, state_out):
+    """(refcount, free_stack, free_count) in and out: out defaults to in (an
+    update in place)."""
+    state_out = state_out if state_out is not None else state_in
+    return tuple(_ptr(t) for t in state_in) + tuple(_ptr(t) for t in state_out)
+
+
+def cow_plan(pages, lengths, path_len, path_nodes, state_in, plan: CowPlan, physical_pages,
+             state_out=None, stream=None):
+    """bc_cow_plan: the batch's copy-on-write bookkeeping on the device.
+    state_in / state_out: (refcount, free_stack, free_count) tensors."""
     batch, max_pages_in = pages.shape
     (po, mpo, lo, cs, cd, er, en, ep, es, cnt) = plan.args()
     _check(_lib.bc_cow_plan(batch, plan.nodes, physical_pages, _ptr(pages), max_pages_in,
-                            _ptr(lengths), _ptr(path_len), _ptr(path_nodes), _ptr(refcount),
-                            _ptr(free_stack), _ptr(free_count), po, mpo, lo, cs, cd, er, en,
-                            ep, es, cnt, _stream(stream)), "bc_cow_plan")
+                            _ptr(lengths), _ptr(path_len), _ptr(path_nodes),
+                            *_state(state_in, state_out), po, mpo, lo, cs, cd, er, en, ep, es,
+                            cnt, _stream(stream)), "bc_cow_plan")
 
 
 def tree_step(shape, draft_q, cache_k, cache_v, pages, lengths, draft_k, draft_v, parent,
-              output, nodes, path_len, path_nodes, refcount, free_stack, free_count,
-              plan: CowPlan, stream=None):
+              output, nodes, path_len, path_nodes, state_in, plan: CowPlan, state_out=None,
+              stream=None):
     """bc_tree_step: device planner, then verify + commit in one launch."""
     (po, mpo, lo, cs, cd, er, en, ep, es, cnt) = plan.args()
     _check(_lib.bc_tree_step(ctypes.byref(shape), _ptr(draft_q), _ptr(cache_k), _ptr(cache_v),
                              _ptr(pages), _ptr(lengths), _ptr(draft_k), _ptr(draft_v),
                              _ptr(parent), _ptr(output), 1 if output.dtype == torch.float16 else 0,
-                             nodes, _ptr(path_len), _ptr(path_nodes), _ptr(refcount),
-                             _ptr(free_stack), _ptr(free_count), po, mpo, lo, cs, cd, er, en, ep,
-                             es, cnt, _stream(stream)), "bc_tree_step")
+                             nodes, _ptr(path_len), _ptr(path_nodes), *_state(state_in, state_out),
+                             po, mpo, lo, cs, cd, er, en, ep, es, cnt, _stream(stream)),
+           "bc_tree_step")
 
 
 def packed_decode(shape, q, packed_kv, pages, lengths, output, block_stride, head_stride,

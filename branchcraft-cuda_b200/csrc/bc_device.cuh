@@ -91,6 +91,36 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// ------------------------------------------------ flags between the CTAs of a grid
+__device__ __forceinline__ void st_release_gpu(int* flag, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* flag) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+  return v;
+}
+
+// Waits until *flag == v (another CTA of this launch publishes it with
+// st_release_gpu); false after kWaitLimitNs, or as soon as another wait of
+// this launch has given up. Only for grids whose CTAs are all resident at
+// once (the publishing CTA must be able to run).
+__device__ __forceinline__ bool wait_flag_gpu(const int* flag, int v) {
+  if (ld_acquire_gpu(flag) == v) return true;
+  const unsigned long long start = globaltimer_ns();
+  const unsigned token = s_launch_token;
+  for (;;) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(flag) == v) return true;
+    if (token != 0u && *reinterpret_cast<volatile unsigned*>(&g_abort_token) == token) return false;
+    if (globaltimer_ns() - start > kWaitLimitNs) {
+      if (token != 0u) atomicExch(&g_abort_token, token);
+      return false;
+    }
+  }
+}
+
 // ------------------------------------------------ programmatic dependent launch
 // A kernel launched with programmatic stream serialization may start while
 // its predecessor in the stream is still running: it must wait here before

@@ -54,6 +54,7 @@
 
 #include "bc_attn.cuh"
 #include "bc_commit.cuh"
+#include "bc_cow_plan.cuh"
 
 namespace bc {
 
@@ -118,6 +119,13 @@ struct TreeParams {
   const int* entry_node;
   const int* entry_page;
   const int* entry_slot;
+  // The planner run inside this launch (plan_inline; one-wave grids only):
+  // one extra cluster (blockIdx.x == plan_item) does no verification; its
+  // first CTA makes the plan with all its threads and publishes
+  // plan.counts[3] = token, which the commit warps of every other CTA wait for.
+  int plan_inline;
+  int plan_item;
+  CowPlanParams plan;
 };
 
 // DUAL: one CTA runs two consecutive 128-row tiles of a request block over
@@ -215,6 +223,21 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
+  if (p.plan_inline && int(blockIdx.x) == p.plan_item) {
+    // ------------------------------------------------------- the planner
+    // The extra cluster: its first CTA plans the batch commit and publishes
+    // the plan to the grid; the others have nothing to do.
+    if (blockIdx.z == 0) {
+      if (tid == 0) s_launch_token = p.token;
+      grid_dependency_wait();  // the plan's inputs and state are visible
+      cow_plan_run<kTreeThreads>(p.plan, tid, [] { __syncthreads(); },
+                                 reinterpret_cast<int*>(smem));
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) st_release_gpu(p.plan.counts + 3, int(p.token));
+    }
+    return;
+  }
 
   // ---- work unit
   const int item = blockIdx.x;
@@ -791,16 +814,27 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     // their last copies, the ancestor sets are written) take the CTA's share
     // of the batch commit's tasks.
     int nclones = p.nclones, nentries = p.nentries;
-    if (p.plan_counts) {  // a plan made on the device by the preceding launch
-      const bool ok = p.plan_counts[2] == 0;
+    bool plan_ready = true;
+    if (p.plan_inline) {
+      CommitScratch& flag_sc = *reinterpret_cast<CommitScratch*>(smem + G::kCommitOff);
+      // (the grid is one wave: the planning CTA is resident and progresses)
+      if (tid == 384) flag_sc.skip = wait_flag_gpu(p.plan.counts + 3, int(p.token)) ? 1u : 0u;
+      named_barrier_sync(4, 128);
+      plan_ready = flag_sc.skip != 0u;
+      named_barrier_sync(4, 128);  // (the scratch is reused by the tasks)
+      if (!plan_ready && tid == 384) atomicOr(p.err, kErrTimeout);
+    }
+    if (p.plan_counts) {  // a plan made on the device (by this launch or the preceding one)
+      const bool ok = plan_ready && p.plan_counts[2] == 0;
       nclones = ok ? min(max(p.plan_counts[0], 0), p.nclones) : 0;
       nentries = ok ? min(max(p.plan_counts[1], 0), p.nentries) : 0;
     }
     CommitScratch& sc = *reinterpret_cast<CommitScratch*>(smem + G::kCommitOff);
-    const int ncta = int(gridDim.x * gridDim.z);
+    const int cols = int(gridDim.x) - (p.plan_inline ? 1 : 0);  // (not the planner's cluster)
+    const int ncta = cols * int(gridDim.z);
     const int row_halves = p.hkv * D;
     const int tasks = 8 * nclones + nentries;
-    for (int task = int(blockIdx.x + gridDim.x * blockIdx.z); task < tasks; task += ncta)
+    for (int task = int(blockIdx.x) + cols * int(blockIdx.z); task < tasks; task += ncta)
       commit_batch_task<128>(task, tid - 384, [] { named_barrier_sync(4, 128); }, sc, row_halves,
                              p.batch, p.nodes, p.physical_pages, p.draft_k, p.draft_v, p.cache_k,
                              p.cache_v, p.clone_src, p.clone_dst, nclones, p.entry_request,

@@ -22,6 +22,8 @@
 #include "bc_tree_mma.cuh"
 #include "branchcraft.h"
 
+static_assert(bc::kCowPlanMaxNodes == BC_MAX_NODES, "the planner's node cap is the API's");
+
 namespace bc {
 
 // Per-device error word (BC_ERR_* bits), set by kernels with atomicOr.
@@ -365,6 +367,32 @@ int tree_splits(int dev, long long items, int tiles) {
   return c;
 }
 
+// The planner as its own single-CTA launch (a programmatic dependent).
+cudaError_t launch_cow_plan(const CowPlanParams& p, cudaStream_t stream) {
+  const size_t smem = cow_plan_smem_bytes(p.batch);
+  static std::atomic<uint64_t> configured{0};
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  if (!(configured.load(std::memory_order_relaxed) & (uint64_t(1) << dev))) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        cow_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        int(cow_plan_smem_bytes(kCowPlanMaxBatch)));
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(uint64_t(1) << dev);
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(kCowPlanThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, cow_plan_kernel, p);
+}
+
 template <int D, bool PREC, bool OUT_HALF, bool DUAL>
 cudaError_t launch_tree_t(TreeParams& p, const CUtensorMap* maps, int items, int tiles,
                           size_t smem, cudaStream_t stream) {
@@ -378,8 +406,27 @@ cudaError_t launch_tree_t(TreeParams& p, const CUtensorMap* maps, int items, int
   // One CTA per SM: a cluster split fits one wave by construction, an
   // unsplit grid when it has no more CTAs than SMs.
   p.early_trigger = (p.splits > 1 || items <= sm_count(dev)) ? 1 : 0;
+  int grid_items = items;
+  if (p.plan_inline == 2) {
+    // A device plan was asked for: made by one extra cluster of this launch
+    // when the grid, that cluster included, is one wave (every CTA resident:
+    // the verification CTAs can wait for the planner), else by the planner
+    // launch, which this one then follows as a programmatic dependent.
+    const bool wave = !DUAL && (p.splits > 1
+                                    ? items + 1 <= tree_max_clusters<D, PREC, OUT_HALF>(dev, p.splits)
+                                    : items + 1 <= sm_count(dev));
+    if (wave && cow_plan_smem_bytes(p.plan.batch) + 1024 <= smem) {
+      p.plan_inline = 1;
+      p.plan_item = items;
+      grid_items = items + 1;
+    } else {
+      p.plan_inline = 0;
+      const cudaError_t e2 = launch_cow_plan(p.plan, stream);
+      if (e2 != cudaSuccess) return e2;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(items), 1, unsigned(p.splits));
+  cfg.gridDim = dim3(unsigned(grid_items), 1, unsigned(p.splits));
   cfg.blockDim = dim3(kTreeThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -409,6 +456,7 @@ struct FusedCommit {
   const int *clone_src, *clone_dst, *entry_request, *entry_node, *entry_page, *entry_slot;
   int nclones, nentries;         // counts, or the capacities of a device-made plan
   const int* plan_counts;        // device-made plan: [clones, entries, status]
+  const CowPlanParams* plan;     // the plan to make first (bc_tree_step)
 };
 
 cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix_k,
@@ -476,6 +524,10 @@ cudaError_t tree_core(const bc_shape* s, const void* draft_q, const void* prefix
     p.nentries = commit->nentries;
     p.commit_tasks = 8 * commit->nclones + commit->nentries;
     p.plan_counts = commit->plan_counts;
+    if (commit->plan) {
+      p.plan = *commit->plan;
+      p.plan_inline = 2;  // (launch_tree_t decides: inside this launch or before it)
+    }
     p.cache_k = static_cast<__half*>(const_cast<void*>(prefix_k));
     p.cache_v = static_cast<__half*>(const_cast<void*>(prefix_v));
     p.draft_k = static_cast<const __half*>(draft_k);
@@ -628,67 +680,54 @@ int bc_tree_verify_commit(const bc_shape* s, const void* draft_q, void* cache_k,
                           const int* entry_page, const int* entry_slot, int nentries,
                           void* stream) {
   const FusedCommit c{clone_src, clone_dst, entry_request, entry_node, entry_page, entry_slot,
-                      nclones, nentries, nullptr};
+                      nclones, nentries, nullptr, nullptr};
   return tree_core(s, draft_q, cache_k, cache_v, pages, lengths, draft_k, draft_v, parent,
                    output, output_f16 != 0, nodes, static_cast<cudaStream_t>(stream), &c);
 }
 
 int bc_cow_plan(int batch, int nodes, int physical_pages, const int* pages_in,
                 int max_pages_in, const int* lengths_in, const int* path_len,
-                const int* path_nodes, int* refcount, int* free_stack, int* free_count,
+                const int* path_nodes, const int* refcount_in, const int* free_stack_in,
+                const int* free_count_in, int* refcount, int* free_stack, int* free_count,
                 int* pages_out, int max_pages_out, int* lengths_out, int* clone_src,
                 int* clone_dst, int* entry_request, int* entry_node, int* entry_page,
                 int* entry_slot, int* counts, void* stream) {
-  if (batch < 1 || nodes < 1 || nodes > BC_MAX_NODES || physical_pages < 1 ||
-      physical_pages > kCowPlanMaxPages || max_pages_in < 1 || max_pages_out < 1 ||
-      !pages_in || !lengths_in || !path_len || !path_nodes || !refcount || !free_stack ||
-      !free_count || !pages_out || !lengths_out || !clone_src || !clone_dst || !entry_request ||
+  if (batch < 1 || batch > kCowPlanMaxBatch || nodes < 1 || nodes > BC_MAX_NODES ||
+      physical_pages < 1 || max_pages_in < 1 || max_pages_out < 1 ||
+      !pages_in || !lengths_in || !path_len || !path_nodes || !refcount_in || !free_stack_in ||
+      !free_count_in || !refcount || !free_stack || !free_count || !pages_out || !lengths_out || !clone_src || !clone_dst || !entry_request ||
       !entry_node || !entry_page || !entry_slot || !counts ||
       (long long)batch * nodes > 0x7fffffffLL || (long long)batch * max_pages_out > 0x7fffffffLL)
     return cudaErrorInvalidValue;
-  const size_t smem = size_t(2) * physical_pages * sizeof(int);
-  static std::atomic<uint64_t> configured{0};
-  const int dev = current_device();
-  if (dev < 0) return cudaErrorInvalidDevice;
-  if (!(configured.load(std::memory_order_relaxed) & (uint64_t(1) << dev))) {
-    const cudaError_t e = cudaFuncSetAttribute(cow_plan_kernel,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               int(size_t(2) * kCowPlanMaxPages * sizeof(int)));
-    if (e != cudaSuccess) return e;
-    configured.fetch_or(uint64_t(1) << dev);
-  }
-  CowPlanParams p{batch, nodes, physical_pages, max_pages_in, max_pages_out, pages_in,
-                  lengths_in, path_len, path_nodes, refcount, free_stack, free_count, pages_out,
-                  lengths_out, clone_src, clone_dst, entry_request, entry_node, entry_page,
-                  entry_slot, counts};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1, 1, 1);
-  cfg.blockDim = dim3(kCowPlanThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = static_cast<cudaStream_t>(stream);
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, cow_plan_kernel, p);
+  const CowPlanParams p{batch, nodes, physical_pages, max_pages_in, max_pages_out, pages_in,
+                        lengths_in, path_len, path_nodes, refcount_in, free_stack_in,
+                        free_count_in, refcount, free_stack, free_count, pages_out,
+                        lengths_out, clone_src, clone_dst, entry_request, entry_node,
+                        entry_page, entry_slot, counts};
+  return launch_cow_plan(p, static_cast<cudaStream_t>(stream));
 }
 
 int bc_tree_step(const bc_shape* s, const void* draft_q, void* cache_k, void* cache_v,
                  const int* pages, const int* lengths, const void* draft_k, const void* draft_v,
                  const int* parent, void* output, int output_f16, int nodes, const int* path_len,
-                 const int* path_nodes, int* refcount, int* free_stack, int* free_count,
+                 const int* path_nodes, const int* refcount_in, const int* free_stack_in,
+                 const int* free_count_in, int* refcount, int* free_stack, int* free_count,
                  int* pages_out, int max_pages_out, int* lengths_out, int* clone_src,
                  int* clone_dst, int* entry_request, int* entry_node, int* entry_page,
                  int* entry_slot, int* counts, void* stream) {
-  if (!basic_shape_ok(s) || s->batch > 256) return cudaErrorInvalidValue;
-  int e = bc_cow_plan(s->batch, nodes, s->physical_pages, pages, s->max_pages, lengths, path_len,
-                      path_nodes, refcount, free_stack, free_count, pages_out, max_pages_out,
-                      lengths_out, clone_src, clone_dst, entry_request, entry_node, entry_page,
-                      entry_slot, counts, stream);
-  if (e != cudaSuccess) return e;
+  if (!basic_shape_ok(s) || s->batch > kCowPlanMaxBatch || nodes < 1 || nodes > BC_MAX_NODES ||
+      max_pages_out < 1 || !path_len || !path_nodes ||
+      !refcount_in || !free_stack_in || !free_count_in || !refcount || !free_stack ||
+      !free_count || !pages_out || !lengths_out || !clone_src || !clone_dst || !entry_request ||
+      !entry_node || !entry_page || !entry_slot || !counts)
+    return cudaErrorInvalidValue;
+  const CowPlanParams plan{s->batch, nodes, s->physical_pages, s->max_pages, max_pages_out,
+                           pages, lengths, path_len, path_nodes, refcount_in, free_stack_in,
+                           free_count_in, refcount, free_stack, free_count, pages_out,
+                           lengths_out, clone_src, clone_dst, entry_request, entry_node,
+                           entry_page, entry_slot, counts};
   const FusedCommit c{clone_src, clone_dst, entry_request, entry_node, entry_page, entry_slot,
-                      s->batch, s->batch * nodes, counts};
+                      s->batch, s->batch * nodes, counts, &plan};
   return tree_core(s, draft_q, cache_k, cache_v, pages, lengths, draft_k, draft_v, parent,
                    output, output_f16 != 0, nodes, static_cast<cudaStream_t>(stream), &c);
 }

@@ -152,9 +152,11 @@ int bc_tree_verify_commit(const bc_shape* shape, const void* draft_q, void* cach
  * the refcount / free-list / clone decisions of the reference's
  * PagedTreeCache.commit (python/branchcraft_torch/transaction.py:114-150),
  * request b committing path_nodes[b, 0 .. path_len[b]) in batch order.
- * State, updated in place: refcount[P], free_stack[0 .. *free_count) (the
- * free list; its last entry is popped first, released pages are pushed) and,
- * per request, pages_in [batch, max_pages_in] / lengths_in [batch] (read).
+ * State: refcount[P], free_stack[0 .. *free_count) (the free list; its last
+ * entry is popped first, released pages are pushed), read from the *_in
+ * arrays and written to refcount / free_stack / free_count (the same arrays
+ * for an update in place, or others to keep the state before), and, per
+ * request, pages_in [batch, max_pages_in] / lengths_in [batch] (read).
  * Writes the page tables after the commit (pages_out [batch, max_pages_out],
  * -1 past each row's end; lengths_out), the plan — clone_src / clone_dst
  * (capacity batch) and entry_request / entry_node / entry_page / entry_slot
@@ -162,30 +164,36 @@ int bc_tree_verify_commit(const bc_shape* shape, const void* draft_q, void* cach
  * (clones, entries, status). status 0: planned; 1: a path empty, longer than
  * `nodes` or with a node id out of range; 2: not enough free pages (the
  * reference's RuntimeError); 3: a malformed table or length. On a nonzero
- * status the state is left unchanged and the plan is empty. P at most 24,576
- * pages (the state is staged in shared memory). One single-CTA launch. Not in
- * the reference (whose bookkeeping is host Python). */
+ * status the state written equals the state read and the plan is empty. batch
+ * at most 256. One single-CTA launch. Not in the reference (whose bookkeeping
+ * is host Python). */
 int bc_cow_plan(int batch, int nodes, int physical_pages, const int* pages_in,
                 int max_pages_in, const int* lengths_in, const int* path_len,
-                const int* path_nodes, int* refcount, int* free_stack, int* free_count,
+                const int* path_nodes, const int* refcount_in, const int* free_stack_in,
+                const int* free_count_in, int* refcount, int* free_stack, int* free_count,
                 int* pages_out, int max_pages_out, int* lengths_out, int* clone_src,
                 int* clone_dst, int* entry_request, int* entry_node, int* entry_page,
                 int* entry_slot, int* counts, void* stream);
 
-/* A whole speculative-verification step with no host round trip: bc_cow_plan
- * on the batch's accepted paths, then bc_tree_verify_commit executing that
- * plan (read from the device; a nonzero planner status commits nothing) in the
- * verify launch. Two launches, the second a programmatic dependent of the
- * first. `pages` / `lengths` are the tables before the commit (what the
- * verification reads); the tables after it go to pages_out / lengths_out.
- * shape->batch at most 256. Not in the reference. */
+/* A whole speculative-verification step with no host round trip: the
+ * bc_cow_plan bookkeeping of the batch's accepted paths, then the verification
+ * with the planned commit executed in the same launch, as
+ * bc_tree_verify_commit does (a nonzero planner status commits nothing).
+ * When the verify grid, with one more cluster, is still one wave, that
+ * extra cluster of the verify launch makes the plan and publishes it to the
+ * others through counts[3] (so counts holds 4 ints; start it at zero: each
+ * launch publishes its own nonzero tag); otherwise a planner launch runs
+ * first. `pages` / `lengths` are the tables before the commit
+ * (what the verification reads); the tables after it go to pages_out /
+ * lengths_out. shape->batch at most 256. Not in the reference. */
 int bc_tree_step(const bc_shape* shape, const void* draft_q, void* cache_k, void* cache_v,
                  const int* pages, const int* lengths, const void* draft_k, const void* draft_v,
                  const int* parent, void* output, int output_f16, int nodes,
-                 const int* path_len, const int* path_nodes, int* refcount, int* free_stack,
-                 int* free_count, int* pages_out, int max_pages_out, int* lengths_out,
-                 int* clone_src, int* clone_dst, int* entry_request, int* entry_node,
-                 int* entry_page, int* entry_slot, int* counts, void* stream);
+                 const int* path_len, const int* path_nodes, const int* refcount_in,
+                 const int* free_stack_in, const int* free_count_in, int* refcount,
+                 int* free_stack, int* free_count, int* pages_out, int max_pages_out,
+                 int* lengths_out, int* clone_src, int* clone_dst, int* entry_request,
+                 int* entry_node, int* entry_page, int* entry_slot, int* counts, void* stream);
 
 /* Decode straight from a packed cache with logical shape [P, Hkv, 16, 2D]:
  * K of (page, kv head, slot) starts at page*block_stride + head*head_stride +

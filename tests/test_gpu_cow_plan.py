@@ -48,7 +48,7 @@ def _run_device(capi, pool, reqs, paths, nodes, width_in, width_out):
     rc, stack, nfree = _device_state(pool)
     pages, lengths, plen, pn = _batch_inputs(pool, reqs, paths, nodes, width_in)
     plan = capi.CowPlan(len(reqs), nodes, width_out)
-    capi.cow_plan(pages, lengths, plen, pn, rc, stack, nfree, plan, pool.physical_pages)
+    capi.cow_plan(pages, lengths, plen, pn, (rc, stack, nfree), plan, pool.physical_pages)
     torch.cuda.synchronize()
     return plan, rc, stack, nfree
 
@@ -120,7 +120,7 @@ def test_bad_paths_change_nothing(capi):
     b = pool.fork(a)
     for paths in ([[0], []], [[0, 9], [1]], [[0] * 8, [1]]):
         plan, rc, stack, nfree = _run_device(capi, pool, [a, b], paths, 7, 2, 4)
-        assert plan.counts.tolist() == [0, 0, 1]
+        assert plan.counts.tolist()[:3] == [0, 0, 1]
         assert rc.tolist() == pool.refcount
         assert stack[:int(nfree.item())].tolist() == pool.free
 
@@ -131,7 +131,7 @@ def test_exhausted_pool_changes_nothing(capi):
     pool.fork(a)
     c = pool.new(40)            # pages 2, 3, 4: nothing left
     plan, rc, stack, nfree = _run_device(capi, pool, [c, a], [[0], [0]], 7, 3, 4)
-    assert plan.counts.tolist() == [0, 0, 2]  # a's clone needs a free page
+    assert plan.counts.tolist()[:3] == [0, 0, 2]  # a's clone needs a free page
     assert rc.tolist() == pool.refcount and int(nfree.item()) == 0
 
 
@@ -159,10 +159,10 @@ def test_config2_step_from_device_state(capi):
     out = torch.full((wl.batch, wl.nodes, wl.hq, wl.dim), float("nan"), device="cuda")
     capi.last_device_error()
     capi.tree_step(s, t["draft_q"], ck, cv, t["pages"], t["lengths"], t["draft_k"], t["draft_v"],
-                   t["parent"], out, wl.nodes, plen, _i32(pn), rc, stack, nfree, plan)
+                   t["parent"], out, wl.nodes, plen, _i32(pn), (rc, stack, nfree), plan)
     torch.cuda.synchronize()
     assert capi.last_device_error() == 0
-    assert plan.counts.tolist() == [7, sum(len(p) for p in wl.paths), 0]
+    assert plan.counts.tolist()[:3] == [7, sum(len(p) for p in wl.paths), 0]
     ref = torch.empty_like(out)
     capi.tree_verify(s, t["draft_q"], U.to_dev(k0), U.to_dev(v0), t["pages"], t["lengths"],
                      t["draft_k"], t["draft_v"], t["parent"], ref, wl.nodes)
@@ -182,3 +182,90 @@ def test_config2_step_from_device_state(capi):
     assert np.array_equal(U.half_bits(cv), cow.v)
     assert plan.pages_out.tolist() == [cow.pages[r] + [-1] * (wl.max_pages - len(cow.pages[r]))
                                        for r in oreqs]
+
+
+def test_state_out_keeps_the_state_in(capi):
+    """With separate output arrays the input state is left as it was (and a
+    failed batch writes the input state to the outputs)."""
+    pool = PagePool(16)
+    a = pool.new(20)
+    b = pool.fork(a)
+    rc, stack, nfree = _device_state(pool)
+    rc2, stack2, nfree2 = (torch.full_like(x, -7) for x in (rc, stack, nfree))
+    pages, lengths, plen, pn = _batch_inputs(pool, [a, b], [[0, 1], [2]], 7, 2)
+    plan = capi.CowPlan(2, 7, 4)
+    capi.cow_plan(pages, lengths, plen, pn, (rc, stack, nfree), plan, 16,
+                  state_out=(rc2, stack2, nfree2))
+    torch.cuda.synchronize()
+    host = pool.plan_commit_batch([(a, [0, 1], 0), (b, [2], 1)], 7)
+    assert plan.counts.tolist()[:3] == [1, 3, 0] and plan.clone_dst[:1].tolist() == host.clone_dst
+    assert rc.tolist() != pool.refcount  # the input state is untouched
+    assert rc2.tolist() == pool.refcount and stack2[:int(nfree2.item())].tolist() == pool.free
+    # a failed batch: the outputs receive the input state
+    rc3, stack3, nfree3 = (torch.full_like(x, -7) for x in (rc, stack, nfree))
+    pages, lengths, plen, pn = _batch_inputs(pool, [a], [[]], 7, 2)
+    capi.cow_plan(pages, lengths, plen, pn, (rc2, stack2, nfree2), plan, 16,
+                  state_out=(rc3, stack3, nfree3))
+    torch.cuda.synchronize()
+    assert plan.counts.tolist()[:3] == [0, 0, 1]
+    assert rc3.tolist() == rc2.tolist() and nfree3.tolist() == nfree2.tolist()
+
+
+@pytest.mark.parametrize("batch,prefix,pool_pages", [
+    (80, 300, 2048),   # 160 CTAs: more than one wave, so the planner is its own launch
+    (6, 40, 64),       # one wave: planned inside the verify launch
+])
+def test_tree_step_both_planner_placements(capi, batch, prefix, pool_pages):
+    """bc_tree_step where the plan is made inside the verify launch (a one-wave
+    grid) and where it cannot be (a grid of several waves): the same
+    sequential result either way — plan, state and tables equal the host
+    planner's, the cache the oracle's, the output the unfused verify's."""
+    rng = np.random.default_rng(batch + prefix)
+    hq, hkv, dim, nodes = 32, 8, 128, 7
+    pool = PagePool(pool_pages)
+    reqs = []
+    for b in range(batch):  # pairs sharing a prefix, lengths not page-aligned
+        reqs.append(pool.new(prefix + 3 * (b // 2)) if b % 2 == 0 else pool.fork(reqs[-1]))
+    width = max(len(pool.pages[r]) for r in reqs)
+    width_out = width + 2
+    ora = CowOracle(pool_pages, hkv, dim)
+    k0 = U.rand_half(rng, (pool_pages, 16, hkv, dim))
+    v0 = U.rand_half(rng, (pool_pages, 16, hkv, dim))
+    ora.k[:], ora.v[:] = k0, v0
+    parent = U.random_tree_parents(rng, batch, nodes)
+    paths = []
+    for b in range(batch):
+        cur, path = int(rng.integers(0, nodes)), []
+        while cur >= 0:
+            path.append(cur)
+            cur = int(parent[b, cur])
+        paths.append(path[::-1])
+    draft_q = U.rand_half(rng, (batch, nodes, hq, dim))
+    draft_k = U.rand_half(rng, (batch, nodes, hkv, dim))
+    draft_v = U.rand_half(rng, (batch, nodes, hkv, dim))
+    rc, stack, nfree = _device_state(pool)
+    pages, lengths, plen, pn = _batch_inputs(pool, reqs, paths, nodes, width)
+    s = capi.make_shape(batch, hq, hkv, dim, width, pool_pages)
+    t = {"draft_q": U.to_dev(draft_q), "draft_k": U.to_dev(draft_k), "draft_v": U.to_dev(draft_v),
+         "parent": U.to_dev(parent)}
+    ck, cv = U.to_dev(k0), U.to_dev(v0)
+    plan = capi.CowPlan(batch, nodes, width_out)
+    out = torch.full((batch, nodes, hq, dim), float("nan"), device="cuda")
+    capi.last_device_error()
+    capi.tree_step(s, t["draft_q"], ck, cv, pages, lengths, t["draft_k"], t["draft_v"],
+                   t["parent"], out, nodes, plen, pn, (rc, stack, nfree), plan)
+    ref = torch.empty_like(out)
+    capi.tree_verify(s, t["draft_q"], U.to_dev(k0), U.to_dev(v0), pages, lengths, t["draft_k"],
+                     t["draft_v"], t["parent"], ref, nodes)
+    torch.cuda.synchronize()
+    assert capi.last_device_error() == 0
+    assert torch.equal(out, ref)
+    host = pool.plan_commit_batch([(reqs[b], paths[b], b) for b in range(batch)], nodes)
+    _assert_matches(pool, host, reqs, plan, rc, stack, nfree, width_out)
+    # the oracle executes the host plan on the same bytes
+    for src, dst in zip(host.clone_src, host.clone_dst):
+        ora.k[dst], ora.v[dst] = ora.k[src], ora.v[src]
+    for r, n, pg, sl in zip(host.entry_request, host.entry_node, host.entry_page, host.entry_slot):
+        ora.k[pg, sl], ora.v[pg, sl] = draft_k[r, n], draft_v[r, n]
+    assert np.array_equal(U.half_bits(ck), ora.k)
+    assert np.array_equal(U.half_bits(cv), ora.v)
