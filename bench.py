@@ -304,10 +304,15 @@ class Workload:
     higher_is_better = True
     scaling = "weak"
     kernel_launches = 1  # launches per kernel_step
-    graphed = False
 
     def prepare(self):
         """After warm-up, before timing (e.g. capture CUDA graphs)."""
+
+    def step_form(self):
+        return "the step's C-ABI calls issued directly"
+
+    def e2e_form(self):
+        return "sequential: H2D, compute, D2H per step"
 
     def release(self):
         """Drop device memory before the next workload."""
@@ -465,10 +470,24 @@ class TreeCow(Workload):
         if rc != 0:
             raise self.C.BranchcraftError(f"bench step failed with cudaError {rc}")
 
+    # The headline step issues the C-ABI call directly: consecutive steps'
+    # kernels are then programmatic dependents (the next launch's set-up
+    # overlaps the previous one's tail), which graph replays are not. The
+    # graph replay of the same step is timed beside it. The end-to-end loop
+    # either issues each step's copies and call on three streams (config 2:
+    # 1.6 MB of copies a step, bound by PCIe: 28.5 us a step against 32.8
+    # with graphs, measured) or replays one graph per step holding the
+    # previous step's result copy, this step and the next step's input copy
+    # (config 1: small copies, bound by the host's issue of ten runtime calls
+    # a step: 15.5 us against 19.2 with streams).
+    direct_steps = True
+    graph_e2e = False
+
     def prepare(self):
         """One CUDA graph per rotating copy, captured from the step's C-ABI
-        calls (the library's per-device caches are warm by now). The step's
-        launch count is read from the captured graphs: their kernel nodes."""
+        calls (the library's per-device caches are warm by now), and the
+        end-to-end loop's graphs. The step's launch count is read from the
+        captured graphs: their kernel nodes."""
         torch = self.torch
         self.graphs = []
         cap = torch.cuda.Stream()
@@ -484,14 +503,29 @@ class TreeCow(Workload):
         if len(kernels) != 1:
             raise RuntimeError(f"the rotating copies' step graphs differ: {sorted(kernels)}")
         self.launches = kernels.pop()
-        self.graphed = True
+        if self.graph_e2e:
+            self._capture_e2e(cap)
+
+    def step_form(self):
+        return ("the step's C-ABI call issued directly (consecutive steps' kernels are "
+                "programmatic dependents)" if self.direct_steps else
+                "one CUDA graph replay per step (the step's C-ABI calls, captured per rotating "
+                "input copy)")
+
+    def e2e_form(self):
+        if self.graph_e2e:
+            return ("pipelined, one CUDA graph per step: the previous step's result D2H, this "
+                    "step's C-ABI call and the next step's input H2D (three branches); the "
+                    "first H2D and the last D2H outside the graphs, so the region moves one "
+                    "input and one result more than its steps use")
+        return "pipelined: next step's H2D and previous step's D2H overlap the compute"
 
     def device_step(self):
         c = self._next()
-        if self.graphed:
-            self.graphs[c].replay()
-        else:
+        if self.direct_steps:
             self.launch(c)
+        else:
+            self.graphs[c].replay()
 
     def kernel_step(self):
         # the dominant kernel: verify with the fused commit (of the host-made
@@ -499,11 +533,20 @@ class TreeCow(Workload):
         self.launch(self._next(), verify_only=not getattr(self, "fused", False), host_plan=True)
 
     def alt_steps(self):
-        """Other forms of the same step, timed beside the headline one."""
-        if not hasattr(self, "states"):
-            return {}
-        return {"plan made once on the host (bc_tree_verify_commit: one launch)":
-                lambda: self.launch(self._next(), host_plan=True)}
+        """Other forms of the same step, timed beside the headline one:
+        name -> (one step, its launches)."""
+        alts = {}
+        if getattr(self, "graphs", None):
+            if self.direct_steps:
+                alts["the same step replayed from a CUDA graph (one per rotating copy)"] = (
+                    lambda: self.graphs[self._next()].replay(), self.launches)
+            else:
+                alts["the same step's C-ABI call issued directly"] = (
+                    lambda: self.launch(self._next()), self.launches)
+        if hasattr(self, "states"):
+            alts["plan made once on the host (bc_tree_verify_commit: one launch)"] = (
+                lambda: self.launch(self._next(), host_plan=True), 1)
+        return alts
 
     def e2e_step(self):
         c = self._next()
@@ -512,7 +555,53 @@ class TreeCow(Workload):
         self.launch(c)
         self.out_hosts[c].copy_(self.outs[c], non_blocking=True)
 
+    def _capture_e2e(self, cap):
+        """Graph c: D2H of copy c-1's result, the step on copy c, H2D of copy
+        c+1's inputs, as three branches joined at the end (copy c+1's inputs
+        were last read by an earlier graph, copy c-1's result was written by
+        the graph before: both complete, by stream order)."""
+        torch = self.torch
+        n = self.copies
+        h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+        self.e2e_graphs = []
+        for c in range(n):
+            prev, nxt = (c - 1) % n, (c + 1) % n
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                h2d.wait_stream(cap)
+                d2h.wait_stream(cap)
+                with torch.cuda.stream(d2h):
+                    self.out_hosts[prev].copy_(self.outs[prev], non_blocking=True)
+                with torch.cuda.stream(h2d):
+                    self.ios[nxt].buf.copy_(self.ios[nxt].host, non_blocking=True)
+                self.launch(c, cap)
+                cap.wait_stream(d2h)
+                cap.wait_stream(h2d)
+            self.e2e_graphs.append(g)
+        torch.cuda.synchronize()
+
     def e2e_region(self, steps):
+        """`steps` end-to-end steps as a serving loop runs them (see
+        e2e_form); every step's inputs go host-to-device and its result
+        device-to-host inside the timed region. Returns the device time (ms)."""
+        if self.graph_e2e:
+            torch = self.torch
+            main = torch.cuda.current_stream()
+            n = self.copies
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(main)
+            self.ios[0].buf.copy_(self.ios[0].host, non_blocking=True)
+            for i in range(steps):
+                self.e2e_graphs[i % n].replay()
+            last = (steps - 1) % n
+            self.out_hosts[last].copy_(self.outs[last], non_blocking=True)
+            t1.record(main)
+            t1.synchronize()
+            self.rot = steps % n
+            return t0.elapsed_time(t1)
+        return self._e2e_streams(steps)
+
+    def _e2e_streams(self, steps):
         """`steps` end-to-end steps as a serving loop runs them: step i's
         inputs go host-to-device on one copy stream, its result device-to-host
         on another, so copies of neighbouring steps overlap the compute; the
@@ -633,10 +722,11 @@ class TreeCow(Workload):
 
 class TreeOracle(TreeCow):
     """one request, 2048-token prefix in a seeded permutation
-    of a 256-page pool, parents [-1,0,0,1,1,2,2], FP16 output; one CUDA graph
-    (the bc_tree_verify_f16 call) per rotating copy."""
+    of a 256-page pool, parents [-1,0,0,1,1,2,2], FP16 output; the step is one
+    bc_tree_verify_f16 call (its graph replay timed beside it)."""
 
     name = "tree-oracle"
+    graph_e2e = True
 
     def __init__(self, torch, C, device, rank, world, **_):
         from bc_workloads import rand_half
@@ -1220,7 +1310,7 @@ class Harness:
             kern.append(region(torch, wl.kernel_step, steps, stream))
         alts = wl.alt_steps() if hasattr(wl, "alt_steps") else {}
         alt_ms = {}
-        for name, fn in alts.items():
+        for name, (fn, _) in alts.items():
             ms = []
             for _ in range(R):
                 self.barrier()
@@ -1268,16 +1358,13 @@ class Harness:
             "value": round(value, 6), "unit": wl.unit, "higher_is_better": wl.higher_is_better,
             "scaling": wl.scaling, "ms_per_step": round(dev_ms / steps, 6),
             "ms_per_step_regions": [round(x / steps, 6) for x in dev],
-            "step_form": ("one CUDA graph replay per step (the step's C-ABI calls, captured "
-                          "per rotating input copy)" if wl.graphed else
-                          "the step's C-ABI calls issued directly"),
+            "step_form": wl.step_form(),
             "config": cfg,
             "e2e": {"value": round(e2e_value, 6), "unit": wl.unit, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms / steps, 6),
-                    "mode": ("pipelined: next step's H2D and previous step's D2H overlap the "
-                             "compute" if hasattr(wl, "e2e_region") else
-                             "sequential: H2D, compute, D2H per step")},
-            "gpu_launches": R * steps * (2 * wl.launches + wl.kernel_launches + len(alt_ms)),
+                    "mode": wl.e2e_form()},
+            "gpu_launches": R * steps * (2 * wl.launches + wl.kernel_launches
+                                         + sum(n for _, n in alts.values())),
             "roofline": roof, "clocks": sampler.window(t0, t1), "device_error_word": err,
         }
         if alt_ms:

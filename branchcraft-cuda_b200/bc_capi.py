@@ -197,7 +197,7 @@ class CowPlan:
         self.entry_node = torch.empty(batch * nodes, **i32)
         self.entry_page = torch.empty(batch * nodes, **i32)
         self.entry_slot = torch.empty(batch * nodes, **i32)
-        self.counts = torch.zeros(4, **i32)  # clones, entries, status, publication tag
+        self.counts = torch.zeros(5, **i32)  # clones, entries, status, publication flag, arrivals
 
     def args(self):
         return (_ptr(self.pages_out), self.max_pages_out, _ptr(self.lengths_out),

@@ -57,7 +57,7 @@ struct CowPlanParams {
   int* entry_node;
   int* entry_page;
   int* entry_slot;
-  int* counts;            // [3]: clones, entries, status
+  int* counts;            // [3]: clones, entries, status ([3], [4]: see plan_flag_arrive)
 };
 
 // Shared memory of one planner run: four scalars, then per request its
@@ -80,6 +80,19 @@ __host__ __device__ inline size_t cow_plan_smem_bytes(int batch) {
 // pushed on the free stack: the batch's pops, in request order (the clone
 // first, then the appended pages), are the stack entries below its top, at
 // offsets given by a prefix sum of each request's pop count.
+// A plan made inside the verification launch is published through
+// counts[3] (0: not yet, 1: published); each of the launch's `participants`
+// (the planning CTA and every CTA that waited for the flag) then arrives
+// here once, after its last read of the flag, and the last one resets
+// counts[3] and counts[4] to zero: the words are zero again when the launch
+// ends, whatever the order in which the CTAs ran.
+__device__ __forceinline__ void plan_flag_arrive(int* counts, int participants) {
+  if (atom_add_acq_rel_gpu(counts + 4, 1) == participants - 1) {
+    counts[3] = 0;
+    counts[4] = 0;
+  }
+}
+
 template <int NT, typename Sync>
 __device__ __forceinline__ int cow_plan_run(const CowPlanParams& p, int t, Sync sync, int* sm) {
   const int B = p.batch, P = p.physical_pages;

@@ -26,7 +26,9 @@ constexpr unsigned long long kWaitLimitNs = 1000000000ull;
 // bounded wait of a launch that gives up stores the launch's token here; every
 // other wait of the same launch, in any CTA and any wave, sees it at its next
 // check and gives up at once, so a systematic stall costs one wait limit, not
-// one per CTA wave. A later launch has another token and is unaffected.
+// one per CTA wave. A later launch has another token and is unaffected (a
+// replayed graph node keeps its token: bc_last_device_error(reset) clears the
+// mark).
 __device__ unsigned g_abort_token;
 __shared__ unsigned s_launch_token;
 
@@ -100,6 +102,13 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* flag) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
   return v;
+}
+
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"
+               : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
 }
 
 // Waits until *flag == v (another CTA of this launch publishes it with

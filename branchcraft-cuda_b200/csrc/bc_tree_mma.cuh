@@ -122,7 +122,10 @@ struct TreeParams {
   // The planner run inside this launch (plan_inline; one-wave grids only):
   // one extra cluster (blockIdx.x == plan_item) does no verification; its
   // first CTA makes the plan with all its threads and publishes
-  // plan.counts[3] = token, which the commit warps of every other CTA wait for.
+  // plan.counts[3] = 1, which the commit warps of every other CTA wait for.
+  // Each of those CTAs and the planner then count themselves in
+  // plan.counts[4]; the last one resets both words to zero, so the next
+  // launch (a replayed graph included) starts from an unpublished flag.
   int plan_inline;
   int plan_item;
   CowPlanParams plan;
@@ -234,7 +237,10 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
                                  reinterpret_cast<int*>(smem));
       __threadfence();
       __syncthreads();
-      if (tid == 0) st_release_gpu(p.plan.counts + 3, int(p.token));
+      if (tid == 0) {
+        st_release_gpu(p.plan.counts + 3, 1);
+        plan_flag_arrive(p.plan.counts, (int(gridDim.x) - 1) * int(gridDim.z) + 1);
+      }
     }
     return;
   }
@@ -818,7 +824,10 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
     if (p.plan_inline) {
       CommitScratch& flag_sc = *reinterpret_cast<CommitScratch*>(smem + G::kCommitOff);
       // (the grid is one wave: the planning CTA is resident and progresses)
-      if (tid == 384) flag_sc.skip = wait_flag_gpu(p.plan.counts + 3, int(p.token)) ? 1u : 0u;
+      if (tid == 384) {
+        flag_sc.skip = wait_flag_gpu(p.plan.counts + 3, 1) ? 1u : 0u;
+        plan_flag_arrive(p.plan.counts, (int(gridDim.x) - 1) * int(gridDim.z) + 1);
+      }
       named_barrier_sync(4, 128);
       plan_ready = flag_sc.skip != 0u;
       named_barrier_sync(4, 128);  // (the scratch is reused by the tasks)

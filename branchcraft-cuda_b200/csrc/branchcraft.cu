@@ -969,8 +969,12 @@ unsigned bc_last_device_error(int reset) {
   unsigned word = 0;
   if (cudaMemcpyFromSymbol(&word, g_error_word, sizeof(word)) != cudaSuccess) return 0xffffffffu;
   if (reset) {
+    // (the abort token too: a captured graph keeps its launches' tokens, so
+    // a replay after a timeout would otherwise find itself aborted)
     const unsigned zero = 0;
-    if (cudaMemcpyToSymbol(g_error_word, &zero, sizeof(zero)) != cudaSuccess) return 0xffffffffu;
+    if (cudaMemcpyToSymbol(g_error_word, &zero, sizeof(zero)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_abort_token, &zero, sizeof(zero)) != cudaSuccess)
+      return 0xffffffffu;
   }
   return word;
 }

@@ -181,9 +181,10 @@ int bc_cow_plan(int batch, int nodes, int physical_pages, const int* pages_in,
  * bc_tree_verify_commit does (a nonzero planner status commits nothing).
  * When the verify grid, with one more cluster, is still one wave, that
  * extra cluster of the verify launch makes the plan and publishes it to the
- * others through counts[3] (so counts holds 4 ints; start it at zero: each
- * launch publishes its own nonzero tag); otherwise a planner launch runs
- * first. `pages` / `lengths` are the tables before the commit
+ * others through counts[3], counting the CTAs that have read it in counts[4]
+ * (so counts holds 5 ints; start [3] and [4] at zero: the launch leaves them
+ * at zero, so a captured graph may be replayed); otherwise a planner launch
+ * runs first. `pages` / `lengths` are the tables before the commit
  * (what the verification reads); the tables after it go to pages_out /
  * lengths_out. shape->batch at most 256. Not in the reference. */
 int bc_tree_step(const bc_shape* shape, const void* draft_q, void* cache_k, void* cache_v,
@@ -291,7 +292,9 @@ int bc_decode_static_scratch(const bc_shape* shape, const void* q, const void* k
 int bc_selftest_bounded_wait(int ctas, int smem_bytes, unsigned limit_us, void* stream);
 
 /* Returns the current device's error word (BC_ERR_* bits; 0 = clean) after
- * synchronising that device; reset != 0 clears it. */
+ * synchronising that device; reset != 0 clears it, and the launch abort mark
+ * (a CUDA graph replays its launches with the tokens they were captured with:
+ * after a BC_ERR_TIMEOUT, clear the word before replaying it). */
 unsigned bc_last_device_error(int reset);
 
 /* Library version string. */

@@ -269,3 +269,83 @@ def test_tree_step_both_planner_placements(capi, batch, prefix, pool_pages):
         ora.k[pg, sl], ora.v[pg, sl] = draft_k[r, n], draft_v[r, n]
     assert np.array_equal(U.half_bits(ck), ora.k)
     assert np.array_equal(U.half_bits(cv), ora.v)
+
+
+def test_tree_step_graph_replays_with_new_paths(capi):
+    """bc_tree_step captured once in a CUDA graph and replayed with other
+    accepted paths written into the same buffers before each replay (the pool
+    state and cache restored): every replay plans its own paths. The plan
+    flag inside the launch must start each replay unpublished (counts[3] and
+    counts[4] are back at zero after every launch), or a replay's commit
+    would read the plan of the replay before."""
+    import copy
+
+    rng = np.random.default_rng(77)
+    batch, prefix, pool_pages = 6, 40, 64
+    hq, hkv, dim, nodes = 32, 8, 128, 7
+    pool = PagePool(pool_pages)
+    reqs = []
+    for b in range(batch):
+        reqs.append(pool.new(prefix + 3 * (b // 2)) if b % 2 == 0 else pool.fork(reqs[-1]))
+    width = max(len(pool.pages[r]) for r in reqs)
+    width_out = width + 2
+    k0 = U.rand_half(rng, (pool_pages, 16, hkv, dim))
+    v0 = U.rand_half(rng, (pool_pages, 16, hkv, dim))
+    parent = U.random_tree_parents(rng, batch, nodes)
+
+    def random_paths():
+        paths = []
+        for b in range(batch):
+            cur, path = int(rng.integers(0, nodes)), []
+            while cur >= 0:
+                path.append(cur)
+                cur = int(parent[b, cur])
+            paths.append(path[::-1])
+        return paths
+
+    draft_q = U.rand_half(rng, (batch, nodes, hq, dim))
+    draft_k = U.rand_half(rng, (batch, nodes, hkv, dim))
+    draft_v = U.rand_half(rng, (batch, nodes, hkv, dim))
+    state_in = _device_state(pool)
+    state_out = tuple(torch.zeros_like(x) for x in state_in)
+    pages, lengths, plen, pn = _batch_inputs(pool, reqs, random_paths(), nodes, width)
+    s = capi.make_shape(batch, hq, hkv, dim, width, pool_pages)
+    t = {"draft_q": U.to_dev(draft_q), "draft_k": U.to_dev(draft_k), "draft_v": U.to_dev(draft_v),
+         "parent": U.to_dev(parent)}
+    k0d, v0d = U.to_dev(k0), U.to_dev(v0)
+    ck, cv = k0d.clone(), v0d.clone()
+    plan = capi.CowPlan(batch, nodes, width_out)
+    out = torch.empty((batch, nodes, hq, dim), device="cuda")
+    capi.last_device_error(reset=True)
+    step = lambda: capi.tree_step(s, t["draft_q"], ck, cv, pages, lengths, t["draft_k"],
+                                  t["draft_v"], t["parent"], out, nodes, plen, pn, state_in,
+                                  plan, state_out=state_out)
+    step()  # warm the library's per-device caches outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(6):
+        paths = random_paths()
+        _, _, plen_h, pn_h = _batch_inputs(pool, reqs, paths, nodes, width)
+        plen.copy_(plen_h)
+        pn.copy_(pn_h)
+        ck.copy_(k0d)
+        cv.copy_(v0d)
+        for x in state_out:
+            x.fill_(-1)
+        g.replay()
+        torch.cuda.synchronize()
+        assert capi.last_device_error() == 0
+        assert plan.counts[3:].tolist() == [0, 0]
+        expect = copy.deepcopy(pool)
+        host = expect.plan_commit_batch([(reqs[b], paths[b], b) for b in range(batch)], nodes)
+        _assert_matches(expect, host, reqs, plan, *state_out, width_out)
+        ka, va = k0.copy(), v0.copy()
+        for src, dst in zip(host.clone_src, host.clone_dst):
+            ka[dst], va[dst] = ka[src], va[src]
+        for r, n, pg, sl in zip(host.entry_request, host.entry_node, host.entry_page,
+                                host.entry_slot):
+            ka[pg, sl], va[pg, sl] = draft_k[r, n], draft_v[r, n]
+        assert np.array_equal(U.half_bits(ck), ka)
+        assert np.array_equal(U.half_bits(cv), va)
