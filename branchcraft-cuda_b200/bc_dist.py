@@ -181,6 +181,7 @@ def exchange_group(ranks=None, timeout_s: float = 30.0):
 
         opts = ProcessGroupNCCL.Options()
         opts.config.blocking = 0
+        opts._timeout = timeout  # (the same value as the kwarg, which wins)
         return dist.new_group(ranks=ranks, timeout=timeout, backend="nccl", pg_options=opts)
     except Exception:
         return dist.new_group(ranks=ranks, timeout=timeout)
