@@ -75,9 +75,11 @@ L2_BYTES = 126 << 20
 # --steps 1..3 --warmup 3 --no-cpu-baseline --no-extras` on a B200. `packed`
 # was captured at --batch 64 (266,106 tokens) and is scaled by tokens to the
 # 256-request batch (1,142,306 tokens): its traffic is a per-token stream.
+# `tree-scale` was captured at --batch 256 (16 of the 64 prefix groups) and is
+# scaled by 4: every group is the same work.
 NCU_TRAFFIC = {
-    "tree-cow": 9176320,
-    "tree-scale": 1880985000 + 514538240,
+    "tree-cow": 9246464,
+    "tree-scale": 4 * (468512768 + 114427648),  # a quarter of the requests, captured
     "decode": 2147777536 + 7383040,
     "packed": round((1092800512 + 7438080) * 1142306 / 266106),
 }
@@ -1051,9 +1053,12 @@ class TreeScale(Workload):
     scaling = "strong"
 
     def __init__(self, torch, C, device, rank, world, total=1024, group=16, prefix=4096,
-                 nodes=63, **_):
+                 nodes=63, batch=0, **_):
         from bc_dist import shard_requests
 
+        # (--batch: fewer requests, whole groups; for small profiling runs)
+        total = max(group, batch // group * group) if batch else total
+        self.total = total
         self.torch, self.C, self.device = torch, C, device
         reqs = shard_requests(total // group, world, rank)  # whole prefix groups
         ngroups = len(reqs)
@@ -1110,8 +1115,9 @@ class TreeScale(Workload):
         return self.flops * steps_all_ranks / seconds / 1e12
 
     def config(self):
-        return {"workload": "BASELINE config 5a: tree_verify, 1024 requests x 63-node full "
-                            "binary trees, 4096-token prefix shared per 16 requests, FP16 out",
+        return {"workload": f"BASELINE config 5a: tree_verify, {self.total} requests x 63-node "
+                            "full binary trees, 4096-token prefix shared per 16 requests, FP16 out"
+                            + ("" if self.total == 1024 else " (a reduced batch, not the config)"),
                 "requests_per_gpu": self.B, "flops_per_step": self.flops,
                 "unique_bytes_per_step": self.unique_bytes,
                 "parallelism": "request-sharded (whole prefix groups)"}
