@@ -1144,11 +1144,13 @@ class TreeScale(Workload):
 class LongCtx(Workload):
     """BASELINE config 5b: one request of 1,048,576 tokens; rank r holds a
     contiguous 1/world shard of its pages and reduces it to FP32 partials
-    (m, l, acc) — `splits` of them per q-head when splits > 8, which a second
-    launch reduces to one partial per q-head (16,640 bytes per rank) — in ONE
-    buffer, which a single NCCL all-gather brings to every rank, where one
-    launch merges all of them (bc_merge_gathered). value = tokens/s (one
-    decoded token per job step); strong scaling."""
+    (m, l, acc), `splits` of them per q-head. With more than one rank, ONE
+    kernel per rank (bc_merge_exchange) reduces them to one state per q-head,
+    writes it into every rank's exchange buffer over NVLink (peer memory,
+    mapped once through CUDA IPC), waits on the device for the peers' flags and
+    merges the world's states; the NCCL form of the same step (reduction, one
+    all-gather of 16,640 bytes per rank, merge) is timed beside it. value =
+    tokens/s (one decoded token per job step); strong scaling."""
 
     name = "longctx"
     unit = "tokens/s"
@@ -1189,16 +1191,16 @@ class LongCtx(Workload):
         self.total = total
         self.kernel_bytes = npg * 16 * 4096 + 32 * 128 * 2 + self.S * 32 * 130 * 4
         self.step_bytes = self.kernel_bytes
-        # partial decode, (world > 1: local reduction to one partial, one NCCL
-        # all-gather,) merge of every rank's partials
-        self.launches = 2 + (world > 1 and self.S > 1)
+        # partial decode, then the exchange kernel (world > 1) or the merge
+        self.launches = 2
         self.kernel = "attn_kernel (paged decode partial)"
         self.bound = "hbm"
-        self.group = None
+        self.group = self.exchange = None
         if world > 1:
-            from bc_dist import exchange_group
+            from bc_dist import PeerExchange, exchange_group
 
             self.group = exchange_group()
+            self.exchange = PeerExchange(32, 128, group=self.group)
 
     def kernel_step(self):
         self.C.paged_decode_partial(self.shape, self.q, self.k, self.v, self.pages, self.lengths,
@@ -1207,16 +1209,26 @@ class LongCtx(Workload):
     def device_step(self):
         self.kernel_step()
         if self.world > 1:
-            import torch.distributed as dist
-
-            if self.S > 1:
-                self.C.merge_to_partial(self.pml, self.pa, self.send_ml[0], self.send_a[0])
-            else:
-                self.buf.copy_(self.part)
-            dist.all_gather_into_tensor(self.gathered, self.buf, group=self.group)
-            self.C.merge_gathered(self.gathered, self.world, 1, 32, 128, self.out)
+            self.exchange.merge(self.pml, self.pa, self.out)
         else:
             self.C.merge_gathered(self.part.view(1, -1), 1, self.S, 32, 128, self.out)
+
+    def nccl_step(self):
+        import torch.distributed as dist
+
+        self.kernel_step()
+        if self.S > 1:
+            self.C.merge_to_partial(self.pml, self.pa, self.send_ml[0], self.send_a[0])
+        else:
+            self.buf.copy_(self.part)
+        dist.all_gather_into_tensor(self.gathered, self.buf, group=self.group)
+        self.C.merge_gathered(self.gathered, self.world, 1, 32, 128, self.out)
+
+    def alt_steps(self):
+        if self.world == 1:
+            return {}
+        return {"the same step with an NCCL all-gather instead of the peer-memory exchange "
+                "(reduction, all_gather_into_tensor, merge)": (self.nccl_step, 2 + (self.S > 1))}
 
     def e2e_step(self):
         self.q.copy_(self.q_host, non_blocking=True)
@@ -1231,13 +1243,17 @@ class LongCtx(Workload):
 
     def config(self):
         return {"workload": "BASELINE config 5b: one request, 1,048,576-token context split "
-                            "across ranks, FP32 partials all-gathered (one NCCL all-gather of "
-                            "one buffer per rank) and merged on the device",
+                            "across ranks, each rank's FP32 partial states sent to every rank "
+                            "over peer memory and merged on the device in one kernel",
                 "tokens_per_gpu": int(self.lengths[0]), "splits_per_gpu": self.splits,
                 "parallelism": f"context-split x{self.world}",
-                "collective_bytes_per_rank": self.buf.numel() * 4 if self.world > 1 else 0}
+                "exchange": ("peer memory (bc_merge_exchange: NVLink stores through CUDA IPC, "
+                             "device-side flags)" if self.world > 1 else "none"),
+                "exchange_bytes_per_rank_to_each_peer": 32 * 132 * 4 if self.world > 1 else 0}
 
     def release(self):
+        if getattr(self, "exchange", None) is not None:
+            self.exchange.close()
         if getattr(self, "group", None) is not None:
             import torch.distributed as dist
 

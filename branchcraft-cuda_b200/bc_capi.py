@@ -31,7 +31,8 @@ EXPORTS = (
     "bc_packed_decode", "bc_packed_decode_kv", "bc_merge_partials",
     "bc_last_device_error", "bc_version", "bc_decode_static_scratch", "bc_merge_gathered",
     "bc_merge_to_partial", "bc_tree_verify_commit", "bc_selftest_bounded_wait",
-    "bc_cow_plan", "bc_tree_step",
+    "bc_cow_plan", "bc_tree_step", "bc_exchange_bytes", "bc_exchange_create",
+    "bc_exchange_open", "bc_exchange_close", "bc_exchange_destroy", "bc_merge_exchange",
 )
 
 
@@ -48,6 +49,7 @@ _vp = ctypes.c_void_p
 _i = ctypes.c_int
 _ll = ctypes.c_longlong
 _f = ctypes.c_float
+_sz = ctypes.c_size_t
 _SP = ctypes.POINTER(Shape)
 
 _sigs = {
@@ -73,6 +75,12 @@ _sigs = {
     "bc_tree_step": [_SP, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp,
                      _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                      _vp],
+    "bc_exchange_bytes": [_i, _i, _i],
+    "bc_exchange_create": [_i, _i, _i, ctypes.POINTER(_vp), _vp],
+    "bc_exchange_open": [_vp, ctypes.POINTER(_vp)],
+    "bc_exchange_close": [_vp],
+    "bc_exchange_destroy": [_vp],
+    "bc_merge_exchange": [_i, _i, ctypes.c_uint, _i, _i, _i, _vp, _vp, _vp, _vp, _vp],
     "bc_last_device_error": [_i],
     "bc_version": [],
 }
@@ -81,6 +89,7 @@ for _name, _args in _sigs.items():
     _fn.argtypes = _args
     _fn.restype = _i
 _lib.bc_last_device_error.restype = ctypes.c_uint
+_lib.bc_exchange_bytes.restype = _sz
 _lib.bc_version.restype = ctypes.c_char_p
 
 
@@ -257,6 +266,47 @@ def merge_partials(partial_ml, partial_a, out, stream=None):
     splits, rows, dim = partial_a.shape
     _check(_lib.bc_merge_partials(splits, rows, dim, _ptr(partial_ml), _ptr(partial_a),
                                   _ptr(out), _stream(stream)), "bc_merge_partials")
+
+
+def exchange_bytes(world, rows, dim) -> int:
+    return int(_lib.bc_exchange_bytes(world, rows, dim))
+
+
+def exchange_create(world, rows, dim):
+    """This rank's exchange buffer (device pointer, int) and its CUDA IPC
+    handle (64 bytes) for the peers."""
+    buf = _vp()
+    handle = ctypes.create_string_buffer(64)
+    _check(_lib.bc_exchange_create(world, rows, dim, ctypes.byref(buf), handle),
+           "bc_exchange_create")
+    return int(buf.value), handle.raw
+
+
+def exchange_open(handle: bytes) -> int:
+    """A peer's exchange buffer mapped into this process (device pointer)."""
+    ptr = _vp()
+    h = ctypes.create_string_buffer(bytes(handle), 64)
+    _check(_lib.bc_exchange_open(h, ctypes.byref(ptr)), "bc_exchange_open")
+    return int(ptr.value)
+
+
+def exchange_close(ptr: int):
+    _check(_lib.bc_exchange_close(_vp(ptr)), "bc_exchange_close")
+
+
+def exchange_destroy(ptr: int):
+    _check(_lib.bc_exchange_destroy(_vp(ptr)), "bc_exchange_destroy")
+
+
+def merge_exchange(world, rank, epoch, partial_ml, partial_a, peers, out, stream=None):
+    """bc_merge_exchange: partial_ml [S, rows, 2], partial_a [S, rows, dim]
+    (this rank's split partials), peers: int64 device tensor of the world's
+    exchange buffers in rank order; out [rows, dim] receives the merge of
+    every rank's partials."""
+    splits, rows, dim = partial_a.shape
+    _check(_lib.bc_merge_exchange(world, rank, epoch, splits, rows, dim, _ptr(partial_ml),
+                                  _ptr(partial_a), _ptr(peers), _ptr(out), _stream(stream)),
+           "bc_merge_exchange")
 
 
 def merge_to_partial(partial_ml, partial_a, out_ml, out_a, stream=None):

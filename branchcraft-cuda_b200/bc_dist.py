@@ -32,6 +32,14 @@ of a multi-GPU deployment of it):
 The compute steps are parameters so the exchange protocol can be exercised on
 CPU ranks (gloo) with a numpy stand-in; the production path passes the CUDA
 entry points of bc_capi.
+
+`PeerExchange` + `p2p_split_kv_decode` replace the all-gather with peer
+memory: one kernel per rank (bc_merge_exchange) reduces the rank's splits,
+writes the reduced state into every rank's exchange buffer over NVLink
+(CUDA IPC mappings made once), waits for the peers' flags on the device
+(bounded: BC_ERR_TIMEOUT, checked by `PeerExchange.check`) and merges the
+world's states — no collective library call on the data path. The handles
+are exchanged once through the process group (any backend).
 """
 from __future__ import annotations
 
@@ -235,4 +243,91 @@ def cuda_split_kv_decode(shape, q, k, v, pages, lengths, group=None, splits: int
         return out
 
     out = split_kv_decode(local_partial, merge, all_gather, 1, rows, shape.dim, world)
+    return out.view(shape.batch, shape.query_heads, shape.dim)
+
+
+class PeerExchange:
+    """The peer-memory exchange of one context split: this rank's exchange
+    buffer, the peers' buffers mapped through CUDA IPC, and the device array
+    of their addresses in rank order. One per (group, rows, dim); `merge`
+    runs one step (every rank calls it the same number of times); `close`
+    unmaps and frees after every rank's last step."""
+
+    def __init__(self, rows: int, dim: int, group=None, capi=None, device=None):
+        import torch
+        import torch.distributed as dist
+
+        self.C = capi if capi is not None else __import__("bc_capi")
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows, self.dim = rows, dim
+        self.own, handle = self.C.exchange_create(self.world, rows, dim)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.mapped = []
+        ptrs = []
+        for w, h in enumerate(handles):
+            if w == self.rank:
+                ptrs.append(self.own)
+            else:
+                p = self.C.exchange_open(h)
+                self.mapped.append(p)
+                ptrs.append(p)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64,
+                                  device=device if device is not None else torch.cuda.current_device())
+        self.epoch = 0
+
+    def merge(self, partial_ml, partial_a, out, stream=None):
+        """One step: this rank's [S, rows, 2] / [S, rows, dim] partials in, the
+        merge of every rank's partials in `out` [rows, dim]."""
+        self.epoch += 1
+        self.C.merge_exchange(self.world, self.rank, self.epoch, partial_ml, partial_a,
+                              self.peers, out, stream)
+
+    def check(self):
+        """Raises CollectiveFailed when a device-side wait for a peer gave up
+        (synchronises the device)."""
+        err = self.C.last_device_error(reset=True)
+        if err & 8:  # BC_ERR_TIMEOUT
+            raise CollectiveFailed(
+                f"rank {self.rank}: a peer's partials did not arrive within the wait limit "
+                f"(device error word {err:#x})")
+        return err
+
+    def close(self):
+        """Unmap the peers' buffers, wait for every rank to stop writing into
+        this one, free it."""
+        import torch
+        import torch.distributed as dist
+
+        if self.peers.is_cuda:
+            torch.cuda.synchronize()
+        for p in self.mapped:
+            self.C.exchange_close(p)
+        self.mapped = []
+        dist.barrier(group=self.group)
+        if self.own:
+            self.C.exchange_destroy(self.own)
+            self.own = 0
+
+
+def p2p_split_kv_decode(shape, q, k, v, pages, lengths, exchange: PeerExchange,
+                        splits: int = 37, gate: StepGate = None, step: int = 0):
+    """Production path over peer memory: bc_paged_decode_partial on this
+    rank's shard (`splits` > 8: every split keeps its partial), then ONE
+    bc_merge_exchange launch (local reduction, the exchange, the merge);
+    returns FP32 [B, Hq, D] on every rank."""
+    import torch
+
+    C = exchange.C
+    rows = shape.batch * shape.query_heads
+    if gate is not None:
+        gate.enter(step)
+    S = splits if splits > 8 else 1  # (up to 8 splits merge in a cluster: one partial)
+    part = torch.empty(block_floats(S, rows, shape.dim), device=q.device, dtype=torch.float32)
+    pml, pa = block_views(part, S, rows, shape.dim)
+    C.paged_decode_partial(shape, q, k, v, pages, lengths, pml, pa, splits)
+    out = torch.empty(rows, shape.dim, device=q.device, dtype=torch.float32)
+    exchange.merge(pml, pa, out)
     return out.view(shape.batch, shape.query_heads, shape.dim)

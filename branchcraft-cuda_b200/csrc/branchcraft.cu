@@ -14,11 +14,13 @@
 #include <atomic>
 #include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 
 #include "bc_attn.cuh"
 #include "bc_commit.cuh"
 #include "bc_cow_plan.cuh"
+#include "bc_exchange.cuh"
 #include "bc_tree_mma.cuh"
 #include "branchcraft.h"
 
@@ -869,6 +871,70 @@ int bc_merge_to_partial(int splits, int rows, int dim, const float* partial_ml,
     return cudaErrorInvalidValue;
   return launch_merge(dim, rows, splits, partial_ml, partial_a, out_a,
                       static_cast<cudaStream_t>(stream), 0, 0, out_ml);
+}
+
+size_t bc_exchange_bytes(int world, int rows, int dim) {
+  if (world < 1 || world > BC_MAX_EXCHANGE_RANKS || rows < 1 || (dim != 64 && dim != 128))
+    return 0;
+  return dim == 64 ? Exch<64>::bytes(world, rows) : Exch<128>::bytes(world, rows);
+}
+
+int bc_exchange_create(int world, int rows, int dim, void** buffer, void* ipc_handle) {
+  const size_t n = bc_exchange_bytes(world, rows, dim);
+  if (n == 0 || !buffer || !ipc_handle) return cudaErrorInvalidValue;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, n);
+  if (e != cudaSuccess) return e;
+  // zero flags: no epoch (>= 1) is published yet
+  e = cudaMemset(p, 0, n);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return e;
+  }
+  *buffer = p;
+  return cudaSuccess;
+}
+
+int bc_exchange_open(const void* ipc_handle, void** peer_buffer) {
+  if (!ipc_handle || !peer_buffer) return cudaErrorInvalidValue;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  return cudaIpcOpenMemHandle(peer_buffer, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+int bc_exchange_close(void* peer_buffer) {
+  return peer_buffer ? cudaIpcCloseMemHandle(peer_buffer) : cudaErrorInvalidValue;
+}
+
+int bc_exchange_destroy(void* buffer) { return buffer ? cudaFree(buffer) : cudaErrorInvalidValue; }
+
+int bc_merge_exchange(int world, int rank, unsigned epoch, int splits, int rows, int dim,
+                      const float* partial_ml, const float* partial_a, float* const* peer_buffers,
+                      float* out, void* stream) {
+  if (world < 1 || world > BC_MAX_EXCHANGE_RANKS || rank < 0 || rank >= world || epoch == 0 ||
+      splits < 1 || rows < 1 || (dim != 64 && dim != 128) || !partial_ml || !partial_a ||
+      !peer_buffers || !out)
+    return cudaErrorInvalidValue;
+  const int dev = current_device();
+  if (dev < 0) return cudaErrorInvalidDevice;
+  unsigned* err = error_word(dev);
+  if (!err) return cudaErrorInvalidDevice;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned((rows + kExchRowsPerBlock - 1) / kExchRowsPerBlock), 1, 1);
+  cfg.blockDim = dim3(32 * kExchRowsPerBlock, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const unsigned token = next_launch_token();
+  return dim == 64
+             ? cudaLaunchKernelEx(&cfg, exchange_merge_kernel<64>, world, rank, epoch, splits, rows,
+                                  partial_ml, partial_a, peer_buffers, out, token, err)
+             : cudaLaunchKernelEx(&cfg, exchange_merge_kernel<128>, world, rank, epoch, splits,
+                                  rows, partial_ml, partial_a, peer_buffers, out, token, err);
 }
 
 int bc_merge_gathered(int world, int splits, int rows, int dim, const float* gathered,

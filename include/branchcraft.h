@@ -1,7 +1,8 @@
 /* branchcraft (B200 / sm_100a) — C ABI of the attention-over-paged-KV hot path.
  *
  * Every entry point takes plain pointers and sizes, launches on the caller's
- * stream (NULL = legacy default stream), allocates nothing and returns a
+ * stream (NULL = legacy default stream), allocates nothing (except
+ * bc_exchange_create, which makes the multi-GPU exchange buffer) and returns a
  * cudaError_t value: 0 on success, cudaErrorInvalidValue (1) for rejected
  * arguments, otherwise the launch status. Asynchronous device faults surface at
  * the caller's next synchronisation, as with any CUDA launch.
@@ -27,6 +28,8 @@
  */
 #ifndef BRANCHCRAFT_H_
 #define BRANCHCRAFT_H_
+
+#include <stddef.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -247,6 +250,34 @@ int bc_merge_to_partial(int splits, int rows, int dim, const float* partial_ml,
  * math is the reference merge_kernel's (src/paged_gqa.cu:76-106). */
 int bc_merge_gathered(int world, int splits, int rows, int dim, const float* gathered,
                       float* out, void* stream);
+
+/* The context-split merge fused with its exchange over peer memory, for one
+ * process per GPU on GPUs with peer access (NVLink / NVSwitch): each rank's
+ * kernel reduces its `splits` local partials per row (bc_paged_decode_partial
+ * layout) to one state, writes it into every rank's exchange buffer with
+ * peer stores, raises a flag per block of 4 rows in each, waits (at most 1 s,
+ * then BC_ERR_TIMEOUT and zero rows) for the other ranks' flags, and merges
+ * the world's states into out [rows, dim] — the same result on every rank, no
+ * collective library call. Set up once per (world, rows, dim):
+ * bc_exchange_create allocates this rank's buffer of bc_exchange_bytes (the
+ * one allocation of this library; zeroed) and returns its CUDA IPC handle (64
+ * bytes); the ranks exchange handles (any host channel), bc_exchange_open
+ * maps each peer's buffer, and peer_buffers is a DEVICE array of the world's
+ * buffer pointers in rank order (this rank's own buffer at `rank`). Every
+ * rank calls bc_merge_exchange with the same epoch, counting up from 1 per
+ * call. Teardown after every rank's last call: bc_exchange_close of the
+ * mapped peers, bc_exchange_destroy of the own buffer. world at most
+ * BC_MAX_EXCHANGE_RANKS. Not in the reference (which has no multi-GPU path);
+ * the merge math is its merge_kernel's (src/paged_gqa.cu:76-106). */
+#define BC_MAX_EXCHANGE_RANKS 64
+size_t bc_exchange_bytes(int world, int rows, int dim);
+int bc_exchange_create(int world, int rows, int dim, void** buffer, void* ipc_handle);
+int bc_exchange_open(const void* ipc_handle, void** peer_buffer);
+int bc_exchange_close(void* peer_buffer);
+int bc_exchange_destroy(void* buffer);
+int bc_merge_exchange(int world, int rank, unsigned epoch, int splits, int rows, int dim,
+                      const float* partial_ml, const float* partial_a,
+                      float* const* peer_buffers, float* out, void* stream);
 
 /* As bc_paged_decode but writing this call's un-merged state as partials
  * (m, l, acc) per (request, q-head) into partial_ml / partial_a, in the layout

@@ -15,8 +15,8 @@ LIB = ROOT / "branchcraft-cuda_b200" / "lib" / "libbranchcraft.so"
 
 def declared():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|unsigned|const char\*)\s+(bc_\w+)\s*\(", text,
-                                 re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|unsigned|size_t|const char\*)\s+(bc_\w+)\s*\(",
+                                 text, re.M)))
 
 
 def test_header_declares_the_boundary():
