@@ -3,7 +3,10 @@ sharding covers every request once, and the split-KV exchange protocol of
 bc_dist (per-rank FP32 (m, l, acc) partials in one buffer -> one all-gather ->
 merge) gives the unsplit decode. The partials here come from a numpy
 restatement; on GPUs the same protocol runs with the CUDA entry points and
-NCCL. The failure tests are in test_dist_failure_cpu.py."""
+NCCL. The peer-memory exchange's host logic (PeerExchange: handle exchange,
+mapping, epochs, teardown) runs here against a recorded C layer; its kernel
+is tested on two GPUs in test_gpu_p2p_exchange.py. The failure tests are in
+test_dist_failure_cpu.py."""
 import os
 import socket
 
@@ -126,3 +129,74 @@ def test_split_kv_exchange_gloo_world2(per_rank):
         assert p.exitcode == 0
     for r in range(2):
         assert np.abs(result[r] - expected).max() < 1e-4
+
+
+class _FakeExchangeC:
+    """The bc_capi calls PeerExchange makes, recorded (no GPU): buffers are
+    numbered 100 + rank, a mapped peer buffer 200 + the peer's rank."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.calls = []
+
+    def exchange_create(self, world, rows, dim):
+        self.calls.append(("create", world, rows, dim))
+        return 100 + self.rank, bytes([self.rank]) * 64
+
+    def exchange_open(self, handle):
+        self.calls.append(("open", handle[0]))
+        return 200 + handle[0]
+
+    def merge_exchange(self, world, rank, epoch, pml, pa, peers, out, stream=None):
+        self.calls.append(("merge", world, rank, epoch, peers.tolist()))
+
+    def last_device_error(self, reset=True):
+        return 0
+
+    def exchange_close(self, ptr):
+        self.calls.append(("close", ptr))
+
+    def exchange_destroy(self, ptr):
+        self.calls.append(("destroy", ptr))
+
+
+def _peer_worker(rank, world, port, result):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from bc_dist import PeerExchange
+
+        C = _FakeExchangeC(rank)
+        ex = PeerExchange(32, 128, capi=C, device="cpu")
+        for _ in range(3):
+            ex.merge(None, None, None)
+        ex.check()
+        ex.close()
+        result[rank] = C.calls
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+def test_peer_exchange_host_logic_gloo_world2():
+    """PeerExchange on CPU ranks with a recorded C layer: every rank maps every
+    other rank's buffer (never its own), passes the world's buffers in rank
+    order, counts the epoch up from 1, and unmaps before it frees its own."""
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    result = manager.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, result)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(100)
+        assert p.exitcode == 0
+    for r in range(2):
+        calls = result[r]
+        other = 1 - r
+        assert calls[0] == ("create", 2, 32, 128)
+        assert calls[1] == ("open", other)
+        peers = [100 + r if w == r else 200 + w for w in range(2)]
+        assert calls[2:5] == [("merge", 2, r, e, peers) for e in (1, 2, 3)]
+        assert calls[5:] == [("close", 200 + other), ("destroy", 100 + r)]
