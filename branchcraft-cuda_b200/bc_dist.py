@@ -287,7 +287,9 @@ class PeerExchange:
 
     def check(self):
         """Raises CollectiveFailed when a device-side wait for a peer gave up
-        (synchronises the device)."""
+        (synchronises the device). The exchange is not reusable after that (a
+        peer may have published an epoch this rank gave up on): close it and
+        build a new one."""
         err = self.C.last_device_error(reset=True)
         if err & 8:  # BC_ERR_TIMEOUT
             raise CollectiveFailed(

@@ -265,7 +265,9 @@ int bc_merge_gathered(int world, int splits, int rows, int dim, const float* gat
  * maps each peer's buffer, and peer_buffers is a DEVICE array of the world's
  * buffer pointers in rank order (this rank's own buffer at `rank`). Every
  * rank calls bc_merge_exchange with the same epoch, counting up from 1 per
- * call. Teardown after every rank's last call: bc_exchange_close of the
+ * call; after a BC_ERR_TIMEOUT the ranks' buffers may hold a half-published
+ * epoch: tear the exchange down and create it again. Teardown after every
+ * rank's last call: bc_exchange_close of the
  * mapped peers, bc_exchange_destroy of the own buffer. world at most
  * BC_MAX_EXCHANGE_RANKS. Not in the reference (which has no multi-GPU path);
  * the merge math is its merge_kernel's (src/paged_gqa.cu:76-106). */
