@@ -349,3 +349,63 @@ def test_tree_step_graph_replays_with_new_paths(capi):
             ka[pg, sl], va[pg, sl] = draft_k[r, n], draft_v[r, n]
         assert np.array_equal(U.half_bits(ck), ka)
         assert np.array_equal(U.half_bits(cv), va)
+
+
+def test_tree_step_serving_loop_on_device_state(capi):
+    """Eight speculative steps of a 6-request batch (pairs sharing prefixes)
+    driven by device state alone: every step's bc_tree_step reads the page
+    tables and the pool state the step before wrote (the state updated in
+    place, the tables from the previous plan's output) and commits into the
+    same cache. After every step the tables and the state equal the host
+    planner's, the output the oracle's verification of the cache as it was
+    before the step, and the cache the bytes of the sequential commits."""
+    rng = np.random.default_rng(123)
+    B, hq, hkv, dim, N, P, W = 6, 8, 2, 64, 7, 160, 24
+    pool = PagePool(P)
+    reqs = []
+    for b in range(B):
+        reqs.append(pool.new(30 + 7 * b) if b % 2 == 0 else pool.fork(reqs[-1]))
+    k_ref = U.rand_half(rng, (P, 16, hkv, dim))
+    v_ref = U.rand_half(rng, (P, 16, hkv, dim))
+    ck, cv = U.to_dev(k_ref), U.to_dev(v_ref)
+    state = _device_state(pool)
+    pages_h = np.array(pool.page_table(reqs, W), np.int32)
+    lens_h = np.array([pool.lengths[r] for r in reqs], np.int32)
+    pages, lengths = _i32(pages_h), _i32(lens_h)
+    s = capi.make_shape(B, hq, hkv, dim, W, P)
+    plans = [capi.CowPlan(B, N, W), capi.CowPlan(B, N, W)]
+    capi.last_device_error(reset=True)
+    for step in range(8):
+        plan = plans[step % 2]  # (the other holds this step's input tables)
+        parent = U.random_tree_parents(rng, B, N)
+        paths = []
+        for b in range(B):
+            cur, path = int(rng.integers(0, N)), []
+            while cur >= 0:
+                path.append(cur)
+                cur = int(parent[b, cur])
+            paths.append(path[::-1])
+        dq = U.rand_half(rng, (B, N, hq, dim))
+        dk = U.rand_half(rng, (B, N, hkv, dim))
+        dv = U.rand_half(rng, (B, N, hkv, dim))
+        _, _, plen, pn = _batch_inputs(pool, reqs, paths, N, W)
+        expected = O.tree((B, hq, hkv, dim, W, P), N, dq, k_ref, v_ref, pages_h, lens_h,
+                          dk, dv, parent)
+        out = torch.empty((B, N, hq, dim), device="cuda")
+        capi.tree_step(s, U.to_dev(dq), ck, cv, pages, lengths, U.to_dev(dk), U.to_dev(dv),
+                       U.to_dev(parent), out, N, plen, pn, state, plan)
+        torch.cuda.synchronize()
+        assert capi.last_device_error() == 0, step
+        host = pool.plan_commit_batch([(reqs[b], paths[b], b) for b in range(B)], N)
+        _assert_matches(pool, host, reqs, plan, *state, W)
+        assert U.max_abs(out.cpu().numpy(), expected) < 2e-4, step
+        for src, dst in zip(host.clone_src, host.clone_dst):
+            k_ref[dst], v_ref[dst] = k_ref[src], v_ref[src]
+        for r, n, pg, sl in zip(host.entry_request, host.entry_node, host.entry_page,
+                                host.entry_slot):
+            k_ref[pg, sl], v_ref[pg, sl] = dk[r, n], dv[r, n]
+        assert np.array_equal(U.half_bits(ck), k_ref), step
+        assert np.array_equal(U.half_bits(cv), v_ref), step
+        # the next step reads the tables this one wrote
+        pages, lengths = plan.pages_out, plan.lengths_out
+        pages_h, lens_h = pages.cpu().numpy(), lengths.cpu().numpy()
