@@ -523,8 +523,11 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
   const bool to_cluster = p.splits > 1;
   const int csize = p.splits;
   const uint32_t rank = to_cluster ? cluster_ctarank() : 0u;
-  const int rpk = (kTreeRows + csize - 1) / csize;  // rows owned by each CTA of the cluster
   const int valid_rows = min(kTreeRows, nreq * p.rows_req - trow * kTreeRows);
+  // Rows owned by each CTA of the cluster in the merge: the tile's valid
+  // rows spread over all its CTAs (a 28-row tile split 8 ways: 4 rows each,
+  // not 16 rows on two CTAs and none on six).
+  const int rpk = (max(valid_rows, 1) + csize - 1) / csize;
   auto out_ptr = [&](int row) -> size_t {
     const int br = trow * kTreeRows + row;
     const int rq = br / p.rows_req, node = (br % p.rows_req) / p.group, hh = br % p.group;
