@@ -1090,7 +1090,7 @@ class TreeScale(Workload):
         self.kernel = "tree_mma_kernel (tree_verify, FP16 out)"
         self.bound = "tensor"
         # end-to-end leg: this step's draft tensors and tables from pinned host
-        # memory, the FP16 verdict tensor back
+        # memory, the FP16 verification output back
         self.host = {n: getattr(self, n).cpu().pin_memory()
                      for n in ("dq", "dk", "dv", "parent", "pages", "lengths")}
         self.out_host = torch.empty(self.out.shape, dtype=torch.float16).pin_memory()

@@ -116,7 +116,7 @@ __device__ __forceinline__ int cow_plan_run(const CowPlanParams& p, int t, Sync 
   }
   for (int b = t; b < B; b += NT) s_last[b] = -1;
   sync();
-  // Round 1 of loads (all independent): lengths, path lengths and nodes, the
+  // First pass of loads (all independent): lengths, path lengths and nodes, the
   // free count, the page rows (copied to the output table; the row's last
   // page kept), and the state copied to the output arrays when they differ.
   if (t == 0) {
@@ -197,7 +197,7 @@ __device__ __forceinline__ int cow_plan_run(const CowPlanParams& p, int t, Sync 
     }
   }
   sync();
-  // Round 2: each request's clone decision (its last page's refcount and its
+  // Second pass: each request's clone decision (its last page's refcount and its
   // rank among the batch's requests with the same last page), and the window
   // of the stack the batch can pop.
   const int win = min(window, max(top0, 0));
