@@ -79,6 +79,10 @@ L2_BYTES = 126 << 20
 # scaled by 4: every group is the same work.
 NCU_TRAFFIC = {
     "tree-cow": 9246464,
+    "tree-oracle": 8603904,
+    # captured at --context 262144: the K/V stream (reads) scales by 4, the
+    # partials (writes) do not
+    "longctx": 4 * 1073859840 + 3932928,
     "tree-scale": 4 * (468512768 + 114427648),  # a quarter of the requests, captured
     "decode": 2147777536 + 7383040,
     "packed": round((1092800512 + 7438080) * 1142306 / 266106),
@@ -1156,8 +1160,10 @@ class LongCtx(Workload):
     unit = "tokens/s"
     scaling = "strong"
 
-    def __init__(self, torch, C, device, rank, world, total=1 << 20, splits=0, **_):
+    def __init__(self, torch, C, device, rank, world, total=1 << 20, splits=0, context=0, **_):
         from bc_dist import block_floats, block_views, shard_pages
+
+        total = context or total  # (--context: a shorter context, for profiling runs)
 
         self.torch, self.C, self.device, self.world = torch, C, device, world
         npg_total = total // 16
@@ -1242,9 +1248,10 @@ class LongCtx(Workload):
         return (steps_all_ranks / self.world) / seconds  # one token per job step
 
     def config(self):
-        return {"workload": "BASELINE config 5b: one request, 1,048,576-token context split "
+        return {"workload": f"BASELINE config 5b: one request, {self.total:,}-token context split "
                             "across ranks, each rank's FP32 partial states sent to every rank "
-                            "over peer memory and merged on the device in one kernel",
+                            "over peer memory and merged on the device in one kernel"
+                            + ("" if self.total == 1 << 20 else " (a shorter context, not the config)"),
                 "tokens_per_gpu": int(self.lengths[0]), "splits_per_gpu": self.splits,
                 "parallelism": f"context-split x{self.world}",
                 "exchange": ("peer memory (bc_merge_exchange: NVLink stores through CUDA IPC, "
@@ -1703,7 +1710,8 @@ def main():
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu-measured DRAM bytes per launch of the dominant kernel, if known")
     ap.add_argument("--batch", type=int, default=0, help="decode/packed batch (0: config's)")
-    ap.add_argument("--context", type=int, default=0, help="decode context tokens (0: 131072)")
+    ap.add_argument("--context", type=int, default=0,
+                    help="decode context tokens (0: 131072); longctx: the context (0: 1,048,576)")
     ap.add_argument("--splits", type=int, default=0, help="decode/longctx KV splits (0: auto)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reference-budget-s", type=float, default=60.0,
