@@ -988,10 +988,7 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
             // rounded to fewer bits), then rounded to FP16: P = hi + lo keeps
             // about 22 bits. (Fewer instructions than a Veltkamp split in
             // FP32: the softmax is issue-bound.)
-            const uint32_t hp = pack_half2(p0, p1);
-            const float2 hf = unpack_half2(hp);
-            ph[e / 2] = hp;
-            pl[e / 2] = pack_half2(__fsub_rn(p0, hf.x), __fsub_rn(p1, hf.y));
+            split_half2(p0, p1, ph[e / 2], pl[e / 2]);
           } else {
             ph[e / 2] = pack_half2(p0, p1);
           }
