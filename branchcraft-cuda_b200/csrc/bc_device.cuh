@@ -210,6 +210,13 @@ __device__ __forceinline__ float2 unpack_half2(uint32_t x) {
 // Splits two FP32 probabilities into an FP16 pair plus an FP16 residual pair:
 // p == hi + lo to about 2^-22 relative, so two FP16 MMAs reproduce an FP32
 // product with V (V is FP16 and exact in both).
+// max of three (one instruction on sm_100: max.f32 with three inputs)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ void split_half2(float p0, float p1, uint32_t& hi, uint32_t& lo) {
   hi = pack_half2(p0, p1);
   const float2 h = unpack_half2(hi);

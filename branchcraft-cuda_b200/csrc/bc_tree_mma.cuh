@@ -951,14 +951,16 @@ __global__ void __launch_bounds__(kTreeThreads, 1)
         }
       }
       float mx;
-      {  // tree reduction: 8 independent partial maxima
+      {  // 8 independent partial maxima of three-input max instructions
         float m8[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) m8[k] = x[k];
-#pragma unroll
-        for (int c = 8; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], x[c]);
-        mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        for (int k = 0; k < 8; ++k) {
+          const float a = fmax3(x[k], x[k + 8], x[k + 16]);
+          const float b = fmax3(a, x[k + 24], x[k + 32]);
+          const float c = fmax3(b, x[k + 40], x[k + 48]);
+          m8[k] = fmaxf(c, x[k + 56]);
+        }
+        mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
         mx *= p.scale_log2;  // -inf stays -inf
       }
       // Lazy max: move the reference only when the max grows by > 8 (log2).
