@@ -409,3 +409,27 @@ def test_tree_step_serving_loop_on_device_state(capi):
         # the next step reads the tables this one wrote
         pages, lengths = plan.pages_out, plan.lengths_out
         pages_h, lens_h = pages.cpu().numpy(), lengths.cpu().numpy()
+
+
+def test_planner_at_its_maximum_sizes(capi):
+    """bc_cow_plan at batch 256 and 256-node paths (the planner's limits):
+    128 shared-prefix pairs with ragged lengths, every request committing a
+    path of up to 256 nodes — the same plan, tables and state as the host
+    planner, bit for bit."""
+    rng = np.random.default_rng(256)
+    B, N = 256, 256
+    P = 8192
+    pool = PagePool(P)
+    reqs = []
+    for b in range(B):
+        reqs.append(pool.new(int(rng.integers(1, 300))) if b % 2 == 0 else pool.fork(reqs[-1]))
+    paths = []
+    for b in range(B):
+        L = int(rng.integers(1, N + 1))
+        paths.append([int(x) for x in rng.choice(N, size=L, replace=False)])
+    width_in = max(len(pool.pages[r]) for r in reqs)
+    width_out = width_in + (N + 15) // 16 + 1
+    plan, rc, stack, nfree = _run_device(capi, pool, reqs, paths, N, width_in, width_out)
+    host = pool.plan_commit_batch([(reqs[b], paths[b], b) for b in range(B)], N)
+    _assert_matches(pool, host, reqs, plan, rc, stack, nfree, width_out)
+    assert plan.counts.tolist()[:3] == [len(host.clone_src), len(host.entry_node), 0]
